@@ -1,0 +1,396 @@
+"""Benchmark of flash_lab's attention path on B200 (prints ONE JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-extra]
+
+Headline workload (BASELINE prefill config): bf16 prefill forward, (B, H, H_kv, S, D) =
+(4, 32, 32, 4096, 128), non-causal, Q/K/V ~ N(0, 1) from a seed, scale 1/sqrt(128). One step is
+one flash_lab.attention call over that batch; metric TFLOP/s counts 4*B*H*S_q*S_k*D FLOP per
+call (the reference's bench/flops.py convention). Inputs (402 MB) are larger than the 126 MB L2,
+so no flush is needed between steps.
+
+  value        whole-job TFLOP/s with inputs resident in HBM (sum over ranks / max rank time)
+  e2e          the same call through the public API with pinned HOST inputs: each step copies
+               q, k, v host->device, runs flash_lab.attention and copies o and lse back
+  roofline     the prefill kernel: achieved FLOP/s from CUDA-event time over the timed region
+               against the measured dense bf16 peak of MEASURED_PEAKS.json; traffic (DRAM bytes
+               per launch) from the committed ncu capture in profiles/ when present
+  cpu_baseline the oracle (numpy fp64 restatement of the reference's flash_lab/reference.py) on
+               this host's cores, on 256 sampled query rows of the same workload (rank 0, N=1)
+  extra        secondary configurations measured the same way on the device: causal prefill,
+               decode B=8 H=H_kv=32 at 32K, GQA decode B=8 H_kv=8 with lengths U[16K, 32K]
+
+Multi-GPU (torchrun, one rank per GPU): every rank runs the full workload on its own GPU with its
+own seed (prefill shards over batch x heads with no communication), so scaling is weak.
+
+--impl reference times the reference's own CPU implementation of the path (the oracle port: the
+reference is Python and cannot travel to this box) on rank 0 only, with all host threads.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "flash-attention-lab_b200"))
+sys.path.insert(0, str(ROOT))
+
+PREFILL = dict(batch=4, heads=32, heads_kv=32, seqlen=4096, head_dim=128)
+METRIC = "prefill TFLOP/s @(4,32,32,4096,128) bf16; decode HBM GB/s @32K cache"
+CPU_SAMPLE_ROWS = 256
+
+
+def prefill_flops(batch, heads, seqlen_q, seqlen_k, head_dim, causal) -> float:
+    f = 4.0 * batch * heads * seqlen_q * seqlen_k * head_dim
+    return f / 2 if causal else f
+
+
+def decode_bytes(heads, heads_kv, head_dim, lens, batch) -> float:
+    """K and V rows of every sequence read once, plus q read and o written (2-byte elements)."""
+    return 2.0 * heads_kv * head_dim * 2 * float(sum(lens)) + 2.0 * batch * heads * head_dim * 2
+
+
+def load_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": data["hbm_gbs"], "bf16_tflops": data["bf16_tflops"],
+                "bf16_tflops_sustained": data.get("bf16_tflops_sustained"),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+            "source": "fallback"}
+
+
+def load_traffic() -> dict:
+    """Per-launch DRAM bytes of each kernel from the committed ncu summary, if any."""
+    path = ROOT / "profiles" / "traffic.json"
+    if path.exists():
+        return json.loads(path.read_text())
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self.thread is not None:
+                self.thread.join(timeout=2)
+
+    def summary(self) -> dict:
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() in ("active", "1"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def time_steps(fn, steps: int, warmup: int, dist=None, device=None):
+    """Runs fn warmup times, then times exactly `steps` calls between CUDA events with a barrier
+    and a synchronize on both sides. Returns (ms per step, max over ranks)."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(device)
+    if dist is not None:
+        dist.barrier()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn()
+    end.record()
+    torch.cuda.synchronize(device)
+    if dist is not None:
+        dist.barrier()
+    ms = start.elapsed_time(end) / steps
+    if dist is not None:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
+def cpu_baseline_prefill(rows: int = CPU_SAMPLE_ROWS) -> dict:
+    """The oracle (numpy fp64) on `rows` sampled query rows of the prefill workload."""
+    import numpy as np
+
+    import oracle
+
+    rng = np.random.default_rng(0)
+    b, h, s, d = PREFILL["batch"], PREFILL["heads"], PREFILL["seqlen"], PREFILL["head_dim"]
+    q = rng.standard_normal((b, s, h, d)).astype(np.float32)
+    k = rng.standard_normal((b, s, h, d)).astype(np.float32)
+    v = rng.standard_normal((b, s, h, d)).astype(np.float32)
+    sample = np.sort(rng.choice(s, size=rows, replace=False))
+    t0 = time.perf_counter()
+    oracle.attention_rows(q, k, v, sample, causal=False, softmax_scale=1 / math.sqrt(d))
+    dt = time.perf_counter() - t0
+    flops = 4.0 * b * h * rows * s * d
+    cores = len(os.sched_getaffinity(0))
+    return {"value": flops / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": f"oracle.attention_rows, {rows} of 4096 query rows x all 128 (b,h), "
+                      f"non-causal, fp64 numpy (BLAS threads = host cores), {dt:.2f} s",
+            "seconds": dt}
+
+
+def run_reference_arm(args) -> None:
+    """--impl reference: the oracle port of the reference's CPU path, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    times = []
+    for _ in range(max(args.warmup, 0)):
+        cpu_baseline_prefill(rows=32)
+    for _ in range(args.steps):
+        times.append(cpu_baseline_prefill(rows=32))
+    value = statistics.median(t["value"] for t in times)
+    sec = statistics.median(t["seconds"] for t in times)
+    b = PREFILL
+    full_ms = prefill_flops(b["batch"], b["heads"], b["seqlen"], b["seqlen"], b["head_dim"],
+                            False) / (value * 1e12) * 1e3
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": full_ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": "prefill (B,H,H_kv,S,D)=(4,32,32,4096,128) non-causal",
+                   "sample": "32 query rows per step (all 128 (b,h), 4096 keys)",
+                   "ms_per_step_is": "extrapolated time of one full call at the sampled rate"},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": times[0]["cores"],
+                         "kind": "port", "sample": times[0]["sample"] + f"; median {sec:.2f} s"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-extra", action="store_true", help="skip the secondary configurations")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return 0
+
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as tdist
+
+        torch.cuda.set_device(local_rank)
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                 device_id=torch.device("cuda", local_rank))
+        dist = tdist
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+
+    import flash_lab
+    from flash_lab import ops
+
+    if not ops.HAS_EXTENSION:
+        raise SystemExit(f"the sm_100a library did not load: {ops.EXTENSION_ERROR}")
+    peaks = load_peaks()
+    traffic = load_traffic()
+
+    b, h, hkv, s, d = (PREFILL[x] for x in ("batch", "heads", "heads_kv", "seqlen", "head_dim"))
+    gen = torch.Generator(device=device).manual_seed(1234 + rank)
+    q = torch.randn(b, s, h, d, device=device, dtype=torch.bfloat16, generator=gen)
+    k = torch.randn(b, s, hkv, d, device=device, dtype=torch.bfloat16, generator=gen)
+    v = torch.randn(b, s, hkv, d, device=device, dtype=torch.bfloat16, generator=gen)
+    scale = 1.0 / math.sqrt(d)
+
+    def step():
+        flash_lab.attention(q, k, v, causal=False, softmax_scale=scale)
+
+    flops = prefill_flops(b, h, s, s, d, False)
+    with ClockSampler(local_rank) as clocks:
+        ms = time_steps(step, args.steps, args.warmup, dist, device)
+    value = world * flops / (ms * 1e-3) / 1e12
+
+    # End to end through the public API with pinned host buffers.
+    hq = q.cpu().pin_memory()
+    hk = k.cpu().pin_memory()
+    hv = v.cpu().pin_memory()
+    ho = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    hl = torch.empty((b, h, s), dtype=torch.float32).pin_memory()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def e2e_step():
+        dq.copy_(hq, non_blocking=True)
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        o, lse = flash_lab.attention(dq, dk, dv, causal=False, softmax_scale=scale,
+                                     return_lse=True)
+        ho.copy_(o, non_blocking=True)
+        hl.copy_(lse, non_blocking=True)
+
+    e2e_ms = time_steps(e2e_step, max(3, args.steps // 4), 3, dist, device)
+    e2e = {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+           "ms_per_step": e2e_ms,
+           "h2d_bytes_per_step": (hq.numel() + hk.numel() + hv.numel()) * 2,
+           "d2h_bytes_per_step": ho.numel() * 2 + hl.numel() * 4}
+
+    achieved = flops / (ms * 1e-3) / 1e12
+    tr = traffic.get("prefill_kernel_noncausal")
+    roofline = {"kernel": "prefill_kernel<bf16> (tcgen05)", "bound": "tensor",
+                "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": achieved / peaks["bf16_tflops"],
+                "traffic": tr.get("bytes_per_launch") if tr else None,
+                "peak_source": f"{peaks['source']} bf16_tflops (burst, kernel timed alone)",
+                "algorithmic": f"{flops:.4e} FLOP per launch (4*B*H*S^2*D)"}
+
+    extra = {}
+    if not args.no_extra:
+        extra = run_extra(torch, flash_lab, device, dist, world, rank, args, peaks, traffic)
+
+    if rank == 0:
+        cpu = None if args.no_cpu or world > 1 else cpu_baseline_prefill()
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": "prefill (B,H,H_kv,S,D)=(4,32,32,4096,128) bf16 non-causal",
+                       "per_gpu_batch": "full config per rank (sharded over batch x heads)",
+                       "l2": "inputs 402 MB > 126 MB L2, no flush", "seed": "1234 + rank"},
+            "clocks": clocks.summary(),
+            "e2e": e2e,
+            "gpu_launches": args.steps,
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "extra": extra,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def run_extra(torch, flash_lab, device, dist, world, rank, args, peaks, traffic) -> dict:
+    """Secondary configurations: causal prefill and the two 32K decode configurations."""
+    out = {}
+    b, h, hkv, s, d = (PREFILL[x] for x in ("batch", "heads", "heads_kv", "seqlen", "head_dim"))
+    gen = torch.Generator(device=device).manual_seed(99 + rank)
+    q = torch.randn(b, s, h, d, device=device, dtype=torch.bfloat16, generator=gen)
+    k = torch.randn(b, s, hkv, d, device=device, dtype=torch.bfloat16, generator=gen)
+    v = torch.randn(b, s, hkv, d, device=device, dtype=torch.bfloat16, generator=gen)
+    flops = prefill_flops(b, h, s, s, d, True)
+    ms = time_steps(lambda: flash_lab.attention(q, k, v, causal=True), args.steps, args.warmup,
+                    dist, device)
+    achieved = flops / (ms * 1e-3) / 1e12
+    out["prefill_causal"] = {"value": world * achieved, "unit": "TFLOP/s", "ms_per_step": ms,
+                             "roofline_frac": achieved / peaks["bf16_tflops"]}
+    del q, k, v
+
+    l2_flush = torch.empty(512 * 2**20, dtype=torch.uint8, device=device)
+    for name, (bb, hh, hk, lens_kind) in {
+        "decode_mha_32k": (8, 32, 32, "full"),
+        "decode_gqa_32k": (8, 32, 8, "ragged"),
+    }.items():
+        smax = 32768
+        gen = torch.Generator(device=device).manual_seed(7 + rank)
+        qd = torch.randn(bb, 1, hh, d, device=device, dtype=torch.bfloat16, generator=gen)
+        kc = torch.randn(bb, smax, hk, d, device=device, dtype=torch.bfloat16, generator=gen)
+        vc = torch.randn(bb, smax, hk, d, device=device, dtype=torch.bfloat16, generator=gen)
+        if lens_kind == "full":
+            lens = [smax] * bb
+        else:
+            lens = torch.randint(16384, smax + 1, (bb,),
+                                 generator=torch.Generator().manual_seed(0)).tolist()
+        seq_lens = torch.tensor(lens, device=device, dtype=torch.int32)
+        nbytes = decode_bytes(hh, hk, d, lens, bb)
+
+        # Kernel-only time with L2 flushed before every call (flush outside the events).
+        times = []
+        for i in range(args.warmup + args.steps):
+            l2_flush.zero_()
+            st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            st.record()
+            flash_lab.decode(qd, kc, vc, seq_lens)
+            en.record()
+            if i >= args.warmup:
+                times.append((st, en))
+        torch.cuda.synchronize(device)
+        ms = statistics.median(st.elapsed_time(en) for st, en in times)
+        if dist is not None:
+            t = torch.tensor([ms], device=device, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"value": world * gbs, "unit": "GB/s", "ms_per_step": ms,
+                     "bytes_per_call": nbytes, "roofline_frac": gbs / peaks["hbm_gbs"],
+                     "peak_gbs": peaks["hbm_gbs"], "config": f"B={bb} H={hh} H_kv={hk} "
+                     f"S_max=32768 D=128 lengths={'32768' if lens_kind == 'full' else lens}",
+                     "l2": "512 MB buffer zeroed before every call (outside the events)"}
+        del qd, kc, vc
+    return out
+
+
+if __name__ == "__main__":
+    sys.exit(main())

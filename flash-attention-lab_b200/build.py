@@ -1,0 +1,101 @@
+"""Builds libflash_lab_b200.so (the C-ABI library) in-tree for sm_100a with nvcc.
+
+    python flash-attention-lab_b200/build.py [--force] [--debug]
+
+Every .cu / .cpp under csrc/ is compiled with
+    nvcc -gencode arch=compute_100a,code=sm_100a -O3 -lineinfo -std=c++17 -Xptxas -v
+and linked into flash_lab/libflash_lab_b200.so next to the Python package that loads it. The
+ptxas resource report (registers, spills, shared memory per kernel) goes to
+build/ptxas.txt. Rebuilds only when a source, header or this script is newer than the library.
+"""
+
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import os
+import pathlib
+import shutil
+import subprocess
+import sys
+
+HERE = pathlib.Path(__file__).resolve().parent
+ROOT = HERE.parent
+CSRC = HERE / "csrc"
+INCLUDE = ROOT / "include"
+BUILD = HERE / "build"
+LIB = HERE / "flash_lab" / "libflash_lab_b200.so"
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-I", str(INCLUDE),
+          "-I", str(CSRC), "--expt-relaxed-constexpr"]
+
+
+def nvcc() -> str:
+    path = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not os.path.exists(path):
+        raise RuntimeError("nvcc not found")
+    return path
+
+
+def sources() -> list[pathlib.Path]:
+    return sorted([*CSRC.glob("*.cu"), *CSRC.glob("*.cpp")])
+
+
+def needs_rebuild() -> bool:
+    if not LIB.exists():
+        return True
+    stamp = LIB.stat().st_mtime
+    deps = [*sources(), *CSRC.glob("*.cuh"), *CSRC.glob("*.h"), *INCLUDE.glob("*.h"),
+            pathlib.Path(__file__)]
+    return any(p.stat().st_mtime > stamp for p in deps)
+
+
+def compile_one(src: pathlib.Path, debug: bool) -> tuple[pathlib.Path, str]:
+    obj = BUILD / (src.name + ".o")
+    cmd = [nvcc(), *ARCH, *COMMON, "-c", str(src), "-o", str(obj)]
+    if src.suffix == ".cu":
+        cmd += ["-Xptxas", "-v"]
+    if debug:
+        cmd += ["-DFLB_DEBUG=1"]
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    if proc.returncode != 0:
+        raise RuntimeError(f"nvcc failed on {src.name}:\n{proc.stdout}\n{proc.stderr}")
+    return obj, proc.stderr
+
+
+def build(force: bool = False, debug: bool = False, verbose: bool = False) -> pathlib.Path:
+    if not force and not needs_rebuild():
+        return LIB
+    BUILD.mkdir(exist_ok=True)
+    srcs = sources()
+    with cf.ThreadPoolExecutor(max_workers=min(8, len(srcs))) as pool:
+        results = list(pool.map(lambda s: compile_one(s, debug), srcs))
+    report = "\n".join(f"== {src.name}\n{log}" for src, (_, log) in zip(srcs, results))
+    (BUILD / "ptxas.txt").write_text(report)
+    if verbose:
+        print(report)
+    tmp = LIB.with_suffix(".so.tmp")
+    # The CUDA runtime is linked statically; driver entry points (cuTensorMapEncodeTiled) are
+    # resolved at run time through cudaGetDriverEntryPoint, so the library loads without a GPU.
+    cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *[str(o) for o, _ in results]]
+    proc = subprocess.run(cmd, capture_output=True, text=True)
+    if proc.returncode != 0:
+        raise RuntimeError(f"link failed:\n{proc.stdout}\n{proc.stderr}")
+    os.replace(tmp, LIB)
+    return LIB
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--debug", action="store_true")
+    ap.add_argument("-v", "--verbose", action="store_true")
+    args = ap.parse_args()
+    lib = build(force=args.force, debug=args.debug, verbose=args.verbose)
+    print(lib)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

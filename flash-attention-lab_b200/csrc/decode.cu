@@ -1,0 +1,664 @@
+// Split-KV decode for sm_100a: one new query token per sequence against the first seq_lens[b]
+// rows of a [B, S_max, H_kv, D] cache, read in place through its strides.
+//
+// Reference behaviour: csrc/decode/decode.cu:41-235 of tfan2437/flash-attention-lab (split-KV
+// "flash-decoding" with a fixed-order log-sum-exp merge), DecodeParams in
+// csrc/common/params.h:31-53.
+//
+// B200 design (not a port):
+//  * One CTA = (sequence b, KV head, <=16 query heads of its GQA group, key split). Every query
+//    head that shares the KV head is served by the same CTA, so GQA reads each K/V byte once.
+//  * A producer warp streams 64-key K and V tiles with TMA (128-byte swizzled boxes of
+//    [64 keys x 64 dims]) into a STAGES-deep mbarrier ring; the strided cache is described by a
+//    4-D tensor map, so any row stride (native [B,S,H,D] or the HF [B,H,S,D] static-cache view)
+//    is read in place.
+//  * Four consumer warps each take 16 keys of every tile. The group's query heads are the M rows
+//    of a 16x8x16 warp MMA (rows beyond the group are zero), so Q K^T and P V are tiny tensor-core
+//    GEMMs and the fp32 online softmax (exp2 domain) stays in registers.
+//  * Partial results of the four warps, and then of the splits, are merged in a fixed order, so a
+//    given configuration is bitwise reproducible.
+//  * seq_lens is read on the device only and clamped to [0, S_max]; keys past a sequence's length
+//    get probability 0 and their V values are masked out of the product (unused cache rows may
+//    hold anything, NaN included).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+
+#include "host_common.h"
+#include "sm100.cuh"
+
+namespace flb {
+namespace {
+
+constexpr int kDecodeBK = 64;                       // keys per tile
+constexpr int kDecodeConsumerWarps = 4;             // 16 keys of each tile per warp
+constexpr int kDecodeThreads = (kDecodeConsumerWarps + 1) * 32;
+constexpr int kMaxHeadsPerCta = 16;                 // M of the warp MMA
+constexpr int kMaxSplits = 256;
+
+struct DecodeArgs {
+  const void* q;
+  void* o;
+  float* lse;
+  const int* seq_lens;
+  float* partial_o;   // [B, H, num_splits_total, D] when writing partials
+  float* partial_ml;  // [B, H, num_splits_total, 2]
+  int* status;
+  int64_t q_batch_stride, q_head_stride;
+  int64_t o_batch_stride, o_head_stride;
+  int batch, heads, heads_kv, group, head_chunks, max_seqlen;
+  int num_splits;         // splits of this launch's key window
+  int split_offset;       // index of this launch's first split in the partial arrays
+  int splits_total;       // split dimension of the partial arrays
+  int key_begin, key_end; // absolute key window of this launch
+  int write_partials;     // 0: write o / lse (num_splits must be 1); 1: write partials
+  float scale_log2;
+  TmaCoords kc, vc;
+};
+
+template <int D>
+struct DecodeCfg {
+  static constexpr int kTileBytes = kDecodeBK * D * 2;   // one K or V tile
+  static constexpr int kBoxes = D / 64;                  // 64-wide column boxes per tile
+  static constexpr int kBoxBytes = kDecodeBK * 128;
+  static constexpr int kStages = D == 128 ? 3 : 6;
+  static constexpr int kStageBytes = 2 * kTileBytes;
+  static constexpr int kMergeBytes =
+      kDecodeConsumerWarps * kMaxHeadsPerCta * (D + 2) * 4;
+  static constexpr int kRingBytes = kStages * kStageBytes;
+  static constexpr int kDataBytes = kRingBytes > kMergeBytes ? kRingBytes : kMergeBytes;
+  static constexpr int kSmemBytes = kDataBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ int tma_c(const TmaCoords& c, int slot, int s, int h, int b) {
+  return c.pos_s == slot ? s : (c.pos_h == slot ? h : b);
+}
+
+__device__ __forceinline__ void load_kv_tile(uint8_t* dst, const CUtensorMap* map,
+                                             const TmaCoords& c, uint64_t* bar, int key, int hkv,
+                                             int b, int boxes) {
+  for (int box = 0; box < boxes; ++box) {
+    tma_load_4d(dst + box * (kDecodeBK * 128), map, bar, box * 64, tma_c(c, 1, key, hkv, b),
+                tma_c(c, 2, key, hkv, b), tma_c(c, 3, key, hkv, b));
+  }
+}
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kDecodeThreads)
+    decode_split_kernel(const __grid_constant__ DecodeArgs a,
+                        const __grid_constant__ CUtensorMap tmk,
+                        const __grid_constant__ CUtensorMap tmv) {
+  using Cfg = DecodeCfg<D>;
+  constexpr int kStages = Cfg::kStages;
+  constexpr int kKSteps = D / 16;   // MMA k-steps over head_dim
+  constexpr int kNTiles = D / 8;    // MMA n-tiles over head_dim in P V
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + Cfg::kDataBytes);
+  uint64_t* empty_bar = full_bar + kStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty_bar + kStages);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // Work item: blockIdx.x = split within this launch, blockIdx.y = (b, hkv, head chunk).
+  const int split = blockIdx.x;
+  const int chunk = blockIdx.y % a.head_chunks;
+  const int bk = blockIdx.y / a.head_chunks;
+  const int hkv = bk % a.heads_kv;
+  const int b = bk / a.heads_kv;
+  const int head0 = hkv * a.group + chunk * kMaxHeadsPerCta;
+  const int heads_here = min(kMaxHeadsPerCta, a.group - chunk * kMaxHeadsPerCta);
+
+  // This split's key range: the window clamped to the sequence length, cut into num_splits
+  // ranges that are whole numbers of tiles (the last one shorter).
+  int len = a.seq_lens[b];
+  len = min(max(len, 0), a.max_seqlen);
+  const int lo = max(a.key_begin, 0);
+  const int hi = min(a.key_end, len);
+  const int n = hi - lo;
+  int k0 = 0, k1 = 0;
+  if (n > 0) {
+    const int per = (n + a.num_splits - 1) / a.num_splits;
+    const int per_split = (per + kDecodeBK - 1) / kDecodeBK * kDecodeBK;
+    k0 = lo + split * per_split;
+    k1 = min(hi, k0 + per_split);
+  }
+  const int ntiles = k1 > k0 ? (k1 - k0 + kDecodeBK - 1) / kDecodeBK : 0;
+
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], kDecodeConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const WaitGuard guard{abort_flag, a.status};
+
+  if (warp == kDecodeConsumerWarps) {
+    // ---------------- producer warp ----------------
+    if (lane == 0 && ntiles > 0) {
+      tma_prefetch_desc(&tmk);
+      tma_prefetch_desc(&tmv);
+      for (int t = 0; t < ntiles; ++t) {
+        const int s = t % kStages;
+        if (t >= kStages) {
+          if (!mbar_wait(&empty_bar[s], ((t / kStages) - 1) & 1, guard)) break;
+        }
+        uint8_t* kdst = smem + s * Cfg::kStageBytes;
+        uint8_t* vdst = kdst + Cfg::kTileBytes;
+        mbar_arrive_expect_tx(&full_bar[s], Cfg::kStageBytes);
+        const int key = k0 + t * kDecodeBK;
+        load_kv_tile(kdst, &tmk, a.kc, &full_bar[s], key, hkv, b, Cfg::kBoxes);
+        load_kv_tile(vdst, &tmv, a.vc, &full_bar[s], key, hkv, b, Cfg::kBoxes);
+      }
+      // Do not leave the CTA while copies are still landing in shared memory.
+      const int first_unwaited = ntiles > kStages ? ntiles - kStages : 0;
+      for (int t = first_unwaited; t < ntiles; ++t) {
+        if (!mbar_wait(&full_bar[t % kStages], (t / kStages) & 1, guard)) break;
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumer warps ----------------
+  const int g = lane >> 2;   // fragment row group
+  const int t4 = lane & 3;   // thread in quad
+
+  // Q as the A operand: rows = query heads of the group (zero beyond heads_here).
+  uint32_t qa[kKSteps][4];
+  {
+    const T* qb = static_cast<const T*>(a.q) + static_cast<int64_t>(b) * a.q_batch_stride;
+    const bool r0 = g < heads_here, r1 = g + 8 < heads_here;
+    const T* q0 = qb + static_cast<int64_t>(head0 + g) * a.q_head_stride;
+    const T* q1 = qb + static_cast<int64_t>(head0 + g + 8) * a.q_head_stride;
+#pragma unroll
+    for (int kk = 0; kk < kKSteps; ++kk) {
+      const int c = kk * 16 + 2 * t4;
+      qa[kk][0] = r0 ? *reinterpret_cast<const uint32_t*>(q0 + c) : 0u;
+      qa[kk][1] = r1 ? *reinterpret_cast<const uint32_t*>(q1 + c) : 0u;
+      qa[kk][2] = r0 ? *reinterpret_cast<const uint32_t*>(q0 + c + 8) : 0u;
+      qa[kk][3] = r1 ? *reinterpret_cast<const uint32_t*>(q1 + c + 8) : 0u;
+    }
+  }
+
+  float o_acc[kNTiles][4];
+#pragma unroll
+  for (int j = 0; j < kNTiles; ++j) o_acc[j][0] = o_acc[j][1] = o_acc[j][2] = o_acc[j][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY};  // log2-domain running max, rows g and g + 8
+  float l_run[2] = {0.f, 0.f};              // this thread's share of the row sums
+
+  const uint32_t smem_base = smem_u32(smem);
+  // ldmatrix row addresses (lane-dependent parts), see sw128_offset.
+  const uint32_t k_row = static_cast<uint32_t>(warp * 16 + (lane >> 4) * 8 + (lane & 7));
+  const uint32_t k_chunk_lo = static_cast<uint32_t>((lane >> 3) & 1);
+  const uint32_t v_row = static_cast<uint32_t>(warp * 16 + ((lane >> 3) & 1) * 8 + (lane & 7));
+  const uint32_t v_chunk_lo = static_cast<uint32_t>(lane >> 4);
+
+  bool ok = true;
+  for (int t = 0; t < ntiles; ++t) {
+    const int s = t % kStages;
+    if (!mbar_wait(&full_bar[s], (t / kStages) & 1, guard)) {
+      ok = false;
+      break;
+    }
+    const uint32_t kbase = smem_base + s * Cfg::kStageBytes;
+    const uint32_t vbase = kbase + Cfg::kTileBytes;
+    const int key_w = k0 + t * kDecodeBK + warp * 16;   // first key of this warp's slice
+    const int valid = k1 - key_w;                       // keys of the slice before the end
+
+    // S = Q K^T over this warp's 16 keys (two n-tiles of 8 keys).
+    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int kk = 0; kk < kKSteps; ++kk) {
+      const uint32_t chunk = 2 * kk + k_chunk_lo;
+      const uint32_t addr = kbase + (chunk >> 3) * Cfg::kBoxBytes + sw128_offset(k_row, chunk & 7);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(addr, b0, b1, b2, b3);
+      mma_16816<T>(sc[0], qa[kk], b0, b1);
+      mma_16816<T>(sc[1], qa[kk], b2, b3);
+    }
+
+    // Online softmax in the exp2 domain; keys at or past k1 are hidden.
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = nt * 8 + 2 * t4 + (e & 1);
+        const float v = key < valid ? sc[nt][e] * a.scale_log2 : -INFINITY;
+        sc[nt][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      }
+    }
+    float ref[2], resc[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+      const float m_new = fmaxf(m_run[r], mx[r]);
+      ref[r] = m_new == -INFINITY ? 0.f : m_new;
+      resc[r] = ex2(m_run[r] - ref[r]);
+      m_run[r] = m_new;
+    }
+    float p[2][4];
+    float psum[2] = {0.f, 0.f};
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        p[nt][e] = ex2(sc[nt][e] - ref[e >> 1]);
+        psum[e >> 1] += p[nt][e];
+      }
+    }
+    l_run[0] = l_run[0] * resc[0] + psum[0];
+    l_run[1] = l_run[1] * resc[1] + psum[1];
+#pragma unroll
+    for (int j = 0; j < kNTiles; ++j) {
+      o_acc[j][0] *= resc[0];
+      o_acc[j][1] *= resc[0];
+      o_acc[j][2] *= resc[1];
+      o_acc[j][3] *= resc[1];
+    }
+    uint32_t pa[4];
+    pa[0] = pack2<T>(p[0][0], p[0][1]);
+    pa[1] = pack2<T>(p[0][2], p[0][3]);
+    pa[2] = pack2<T>(p[1][0], p[1][1]);
+    pa[3] = pack2<T>(p[1][2], p[1][3]);
+
+    // V rows of hidden keys are masked to zero in the B fragments (0 * NaN would poison O).
+    // Fragment keys: regs 0/2 hold keys 2*t4 + {0,1}, regs 1/3 keys 8 + 2*t4 + {0,1}.
+    uint32_t vmask_lo = 0xffffffffu, vmask_hi = 0xffffffffu;
+    if (valid < 16) {
+      const int kl = 2 * t4, kh = 8 + 2 * t4;
+      vmask_lo = (kl < valid ? 0x0000ffffu : 0u) | (kl + 1 < valid ? 0xffff0000u : 0u);
+      vmask_hi = (kh < valid ? 0x0000ffffu : 0u) | (kh + 1 < valid ? 0xffff0000u : 0u);
+    }
+#pragma unroll
+    for (int jp = 0; jp < kNTiles / 2; ++jp) {
+      const uint32_t chunk = 2 * jp + v_chunk_lo;
+      const uint32_t addr = vbase + (chunk >> 3) * Cfg::kBoxBytes + sw128_offset(v_row, chunk & 7);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_trans(addr, b0, b1, b2, b3);
+      mma_16816<T>(o_acc[2 * jp], pa, b0 & vmask_lo, b1 & vmask_hi);
+      mma_16816<T>(o_acc[2 * jp + 1], pa, b2 & vmask_lo, b3 & vmask_hi);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[s]);
+  }
+
+  // Full row sums of this warp.
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 1);
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 2);
+  }
+
+  // All consumer warps are past the ring (the producer waited for its last copies), so the ring
+  // memory is reused for the cross-warp merge.
+  asm volatile("bar.sync 1, %0;" ::"n"(kDecodeConsumerWarps * 32) : "memory");
+  if (!ok || *abort_flag) return;
+  float* wm = reinterpret_cast<float*>(smem);                         // [warps][16]
+  float* wl = wm + kDecodeConsumerWarps * kMaxHeadsPerCta;            // [warps][16]
+  float* wo = wl + kDecodeConsumerWarps * kMaxHeadsPerCta;            // [warps][16][D]
+  if (t4 == 0) {
+    wm[warp * kMaxHeadsPerCta + g] = m_run[0];
+    wm[warp * kMaxHeadsPerCta + g + 8] = m_run[1];
+    wl[warp * kMaxHeadsPerCta + g] = l_run[0];
+    wl[warp * kMaxHeadsPerCta + g + 8] = l_run[1];
+  }
+#pragma unroll
+  for (int j = 0; j < kNTiles; ++j) {
+    const int col = j * 8 + 2 * t4;
+    float* r0 = wo + (warp * kMaxHeadsPerCta + g) * D + col;
+    float* r1 = wo + (warp * kMaxHeadsPerCta + g + 8) * D + col;
+    r0[0] = o_acc[j][0];
+    r0[1] = o_acc[j][1];
+    r1[0] = o_acc[j][2];
+    r1[1] = o_acc[j][3];
+  }
+  asm volatile("bar.sync 1, %0;" ::"n"(kDecodeConsumerWarps * 32) : "memory");
+
+  const int tid = threadIdx.x;
+  for (int idx = tid; idx < heads_here * D; idx += kDecodeConsumerWarps * 32) {
+    const int row = idx / D;
+    const int d = idx - row * D;
+    float m = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kDecodeConsumerWarps; ++w) m = fmaxf(m, wm[w * kMaxHeadsPerCta + row]);
+    float num = 0.f, den = 0.f;
+#pragma unroll
+    for (int w = 0; w < kDecodeConsumerWarps; ++w) {
+      const float mw = wm[w * kMaxHeadsPerCta + row];
+      if (mw != -INFINITY) {
+        const float f = ex2(mw - m);
+        num += wo[(w * kMaxHeadsPerCta + row) * D + d] * f;
+        den += wl[w * kMaxHeadsPerCta + row] * f;
+      }
+    }
+    const int h = head0 + row;
+    if (!a.write_partials) {
+      T* o = static_cast<T*>(a.o) + static_cast<int64_t>(b) * a.o_batch_stride +
+             static_cast<int64_t>(h) * a.o_head_stride;
+      const float val = den > 0.f ? num / den : 0.f;
+      if constexpr (sizeof(T) == 2) {
+        if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+          o[d] = __float2bfloat16_rn(val);
+        } else {
+          o[d] = __float2half_rn(val);
+        }
+      }
+      if (d == 0) {
+        a.lse[static_cast<int64_t>(b) * a.heads + h] =
+            den > 0.f ? m * 0.69314718055994530942f + logf(den) : -INFINITY;
+      }
+    } else {
+      const int64_t slot =
+          (static_cast<int64_t>(b) * a.heads + h) * a.splits_total + a.split_offset + split;
+      a.partial_o[slot * D + d] = num;
+      if (d == 0) {
+        a.partial_ml[2 * slot] = m;
+        a.partial_ml[2 * slot + 1] = den;
+      }
+    }
+  }
+}
+
+// Fixed-order merge of the split partials of one (b, h): thread d owns output column d.
+// m = max_s m_s; l = sum_s l_s 2^(m_s - m); o = sum_s o_s 2^(m_s - m) / l (empty splits skipped).
+template <typename T>
+__global__ void decode_merge_kernel(const float* __restrict__ partial_o,
+                                    const float* __restrict__ partial_ml, int heads, int head_dim,
+                                    int num_splits, T* o, int64_t o_batch_stride,
+                                    int64_t o_head_stride, float* lse) {
+  const int bh = blockIdx.x;
+  const int b = bh / heads;
+  const int h = bh - b * heads;
+  const int64_t base = static_cast<int64_t>(bh) * num_splits;
+  float m = -INFINITY;
+  for (int s = 0; s < num_splits; ++s) m = fmaxf(m, partial_ml[2 * (base + s)]);
+  for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
+    float num = 0.f, den = 0.f;
+    for (int s = 0; s < num_splits; ++s) {
+      const float ms = partial_ml[2 * (base + s)];
+      if (ms != -INFINITY) {
+        const float f = ex2(ms - m);
+        num += partial_o[(base + s) * head_dim + d] * f;
+        den += partial_ml[2 * (base + s) + 1] * f;
+      }
+    }
+    const float val = den > 0.f ? num / den : 0.f;
+    T* out = o + static_cast<int64_t>(b) * o_batch_stride + static_cast<int64_t>(h) * o_head_stride;
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      out[d] = __float2bfloat16_rn(val);
+    } else {
+      out[d] = __float2half_rn(val);
+    }
+    if (d == 0) lse[bh] = den > 0.f ? m * 0.69314718055994530942f + logf(den) : -INFINITY;
+  }
+}
+
+template <typename T, int D>
+int launch_split(const DecodeArgs& args, const CUtensorMap& tmk, const CUtensorMap& tmv,
+                 int grid_x, int grid_y, cudaStream_t stream) {
+  using Cfg = DecodeCfg<D>;
+  static thread_local int configured_device = -1;  // per-thread cache of the attribute set-up
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    if (int st = check_cuda(cudaFuncSetAttribute(decode_split_kernel<T, D>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 Cfg::kSmemBytes),
+                            "cudaFuncSetAttribute(decode)"))
+      return st;
+    configured_device = dev;
+  }
+  decode_split_kernel<T, D><<<dim3(grid_x, grid_y), kDecodeThreads, Cfg::kSmemBytes, stream>>>(
+      args, tmk, tmv);
+  return check_cuda(cudaGetLastError(), "decode_split_kernel launch");
+}
+
+template <typename T>
+int launch_merge(const float* po, const float* pml, int batch, int heads, int head_dim,
+                 int splits, void* o, int64_t obs, int64_t ohs, float* lse, cudaStream_t stream) {
+  decode_merge_kernel<T><<<batch * heads, head_dim, 0, stream>>>(
+      po, pml, heads, head_dim, splits, static_cast<T*>(o), obs, ohs, lse);
+  return check_cuda(cudaGetLastError(), "decode_merge_kernel launch");
+}
+
+int validate(const flb_decode_params* p) {
+  if (p == nullptr) return fail(FLB_ERR_INVALID_ARGUMENT, "params is NULL");
+  if (!p->q || !p->k_cache || !p->v_cache || !p->o || !p->lse || !p->seq_lens)
+    return fail(FLB_ERR_INVALID_ARGUMENT, "a required pointer is NULL");
+  if (p->batch <= 0 || p->heads <= 0 || p->heads_kv <= 0 || p->max_seqlen <= 0)
+    return fail(FLB_ERR_INVALID_ARGUMENT, "empty input: batch %d heads %d heads_kv %d S_max %d",
+                p->batch, p->heads, p->heads_kv, p->max_seqlen);
+  if (p->heads % p->heads_kv != 0)
+    return fail(FLB_ERR_INVALID_ARGUMENT,
+                "the number of query heads (%d) must be a multiple of KV heads (%d)", p->heads,
+                p->heads_kv);
+  if (p->dtype != FLB_BF16 && p->dtype != FLB_FP16)
+    return fail(FLB_ERR_UNSUPPORTED, "decode takes bf16 or fp16 (dtype code %d)", p->dtype);
+  if (p->head_dim != 64 && p->head_dim != 128)
+    return fail(FLB_ERR_UNSUPPORTED, "unsupported head_dim %d (64 or 128)", p->head_dim);
+  if (!(p->softmax_scale > 0.f))
+    return fail(FLB_ERR_INVALID_ARGUMENT, "softmax_scale must be positive");
+  if (p->num_splits < 0 || p->num_splits > kMaxSplits)
+    return fail(FLB_ERR_INVALID_ARGUMENT, "num_splits must be in [0, %d]", kMaxSplits);
+  if (reinterpret_cast<uintptr_t>(p->q) % 16 != 0 ||
+      (p->batch > 1 && (p->q_batch_stride * 2) % 16 != 0) ||
+      (p->heads > 1 && (p->q_head_stride * 2) % 16 != 0))
+    return fail(FLB_ERR_MISALIGNED, "q must have 16-byte aligned rows");
+  return FLB_OK;
+}
+
+int build_maps(const flb_decode_params* p, CUtensorMap* tmk, CUtensorMap* tmv, TmaCoords* kc,
+               TmaCoords* vc) {
+  View4 kv{p->k_cache,
+           {p->batch, p->max_seqlen, p->heads_kv, p->head_dim},
+           {p->k_batch_stride, p->k_seq_stride, p->k_head_stride, 1},
+           2};
+  View4 vv{p->v_cache,
+           {p->batch, p->max_seqlen, p->heads_kv, p->head_dim},
+           {p->v_batch_stride, p->v_seq_stride, p->v_head_stride, 1},
+           2};
+  if (!rows_16b_aligned(kv))
+    return fail(FLB_ERR_MISALIGNED, "k_cache must have 16-byte aligned rows (data pointer and strides)");
+  if (!rows_16b_aligned(vv))
+    return fail(FLB_ERR_MISALIGNED, "v_cache must have 16-byte aligned rows (data pointer and strides)");
+  if (int st = encode_rows_x64_map(tmk, kc, kv, kDecodeBK, p->dtype)) return st;
+  return encode_rows_x64_map(tmv, vc, vv, kDecodeBK, p->dtype);
+}
+
+DecodeArgs make_args(const flb_decode_params* p) {
+  DecodeArgs a{};
+  a.q = p->q;
+  a.o = p->o;
+  a.lse = p->lse;
+  a.seq_lens = p->seq_lens;
+  a.status = p->status;
+  a.q_batch_stride = p->q_batch_stride;
+  a.q_head_stride = p->q_head_stride;
+  a.o_batch_stride = p->o_batch_stride;
+  a.o_head_stride = p->o_head_stride;
+  a.batch = p->batch;
+  a.heads = p->heads;
+  a.heads_kv = p->heads_kv;
+  a.group = p->heads / p->heads_kv;
+  a.head_chunks = (a.group + kMaxHeadsPerCta - 1) / kMaxHeadsPerCta;
+  a.max_seqlen = p->max_seqlen;
+  a.scale_log2 = static_cast<float>(static_cast<double>(p->softmax_scale) * 1.4426950408889634);
+  a.key_begin = 0;
+  a.key_end = p->max_seqlen;
+  return a;
+}
+
+template <typename F>
+int dispatch(int dtype, int head_dim, F&& f) {
+  if (dtype == FLB_BF16) {
+    if (head_dim == 128) return f(__nv_bfloat16{}, std::integral_constant<int, 128>{});
+    return f(__nv_bfloat16{}, std::integral_constant<int, 64>{});
+  }
+  if (head_dim == 128) return f(__half{}, std::integral_constant<int, 128>{});
+  return f(__half{}, std::integral_constant<int, 64>{});
+}
+
+int splits_for(int batch, int heads, int heads_kv, int head_dim, int max_seqlen, int sm_count) {
+  if (batch <= 0 || heads <= 0 || heads_kv <= 0 || heads % heads_kv != 0 || max_seqlen <= 0 ||
+      sm_count <= 0)
+    return 1;
+  const int group = heads / heads_kv;
+  const int chunks = (group + kMaxHeadsPerCta - 1) / kMaxHeadsPerCta;
+  const int64_t ctas = static_cast<int64_t>(batch) * heads_kv * chunks;
+  const int per_sm = head_dim == 128 ? 2 : 3;  // resident CTAs per SM for the ring size
+  const int64_t slots = static_cast<int64_t>(sm_count) * per_sm;
+  // At least 4 tiles per split of the longest sequence.
+  const int max_splits =
+      static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(kMaxSplits, max_seqlen / 256)));
+  if (ctas >= 4 * slots) return 1;
+  // Smallest split count giving >= 3 waves with a full-enough last wave; else about 4 waves.
+  for (int s = 1; s <= max_splits; ++s) {
+    const double waves = static_cast<double>(ctas * s) / static_cast<double>(slots);
+    if (waves < 3.0) continue;
+    const double eff = waves / std::ceil(waves);
+    if (eff >= 0.9) return s;
+  }
+  const int64_t want = (4 * slots + ctas - 1) / ctas;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(max_splits, want)));
+}
+
+}  // namespace
+}  // namespace flb
+
+using namespace flb;
+
+extern "C" int flb_decode_num_splits(int32_t batch, int32_t heads, int32_t heads_kv,
+                                     int32_t head_dim, int32_t max_seqlen, int32_t sm_count) {
+  return splits_for(batch, heads, heads_kv, head_dim, max_seqlen, sm_count);
+}
+
+extern "C" size_t flb_decode_workspace_bytes(int32_t batch, int32_t heads, int32_t head_dim,
+                                             int32_t num_splits) {
+  if (num_splits <= 1 || batch <= 0 || heads <= 0 || head_dim <= 0) return 0;
+  const size_t slots = static_cast<size_t>(batch) * heads * num_splits;
+  const size_t o_bytes = (slots * head_dim * sizeof(float) + 255) / 256 * 256;
+  return o_bytes + slots * 2 * sizeof(float);
+}
+
+extern "C" int flb_decode_fwd(const flb_decode_params* p, flb_stream_t stream_) {
+  clear_error();
+  if (int st = validate(p)) return st;
+  int dev = 0, sm_count = 0;
+  if (int st = current_device_info(&dev, &sm_count, nullptr, nullptr)) return st;
+  CUtensorMap tmk, tmv;
+  TmaCoords kc{}, vc{};
+  if (int st = build_maps(p, &tmk, &tmv, &kc, &vc)) return st;
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+
+  DecodeArgs a = make_args(p);
+  a.kc = kc;
+  a.vc = vc;
+  const int splits = p->num_splits > 0
+                         ? p->num_splits
+                         : splits_for(p->batch, p->heads, p->heads_kv, p->head_dim,
+                                      p->max_seqlen, sm_count);
+  const int grid_y = p->batch * p->heads_kv * a.head_chunks;
+  if (grid_y > 65535)
+    return fail(FLB_ERR_UNSUPPORTED, "batch * heads_kv * head chunks = %d exceeds 65535", grid_y);
+  a.num_splits = splits;
+  a.split_offset = 0;
+  a.splits_total = splits;
+  if (splits == 1) {
+    a.write_partials = 0;
+    return dispatch(p->dtype, p->head_dim, [&](auto tag, auto dim) {
+      return launch_split<decltype(tag), decltype(dim)::value>(a, tmk, tmv, 1, grid_y, stream);
+    });
+  }
+  const size_t need = flb_decode_workspace_bytes(p->batch, p->heads, p->head_dim, splits);
+  if (p->workspace == nullptr || p->workspace_bytes < need)
+    return fail(FLB_ERR_WORKSPACE, "decode with %d splits needs %zu bytes of workspace, got %zu",
+                splits, need, p->workspace == nullptr ? size_t(0) : p->workspace_bytes);
+  if (reinterpret_cast<uintptr_t>(p->workspace) % 256 != 0)
+    return fail(FLB_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+  const size_t slots = static_cast<size_t>(p->batch) * p->heads * splits;
+  a.partial_o = static_cast<float*>(p->workspace);
+  a.partial_ml = reinterpret_cast<float*>(static_cast<char*>(p->workspace) +
+                                          (slots * p->head_dim * sizeof(float) + 255) / 256 * 256);
+  a.write_partials = 1;
+  return dispatch(p->dtype, p->head_dim, [&](auto tag, auto dim) {
+    using T = decltype(tag);
+    if (int st = launch_split<T, decltype(dim)::value>(a, tmk, tmv, splits, grid_y, stream))
+      return st;
+    return launch_merge<T>(a.partial_o, a.partial_ml, p->batch, p->heads, p->head_dim, splits,
+                           p->o, p->o_batch_stride, p->o_head_stride, p->lse, stream);
+  });
+}
+
+extern "C" int flb_decode_partials(const flb_decode_params* p, int32_t key_begin,
+                                   int32_t key_end, float* partial_o, float* partial_ml,
+                                   flb_stream_t stream_) {
+  clear_error();
+  if (p == nullptr) return fail(FLB_ERR_INVALID_ARGUMENT, "params is NULL");
+  flb_decode_params q = *p;
+  // o / lse are not written in this mode; accept NULL for them.
+  static char dummy;
+  if (q.o == nullptr) q.o = &dummy;
+  if (q.lse == nullptr) q.lse = reinterpret_cast<float*>(&dummy);
+  if (int st = validate(&q)) return st;
+  if (!partial_o || !partial_ml) return fail(FLB_ERR_INVALID_ARGUMENT, "partials are NULL");
+  if (key_begin < 0 || key_end < key_begin)
+    return fail(FLB_ERR_INVALID_ARGUMENT, "bad key window [%d, %d)", key_begin, key_end);
+  if (q.num_splits < 1) return fail(FLB_ERR_INVALID_ARGUMENT, "num_splits must be >= 1 here");
+  int dev = 0, sm_count = 0;
+  if (int st = current_device_info(&dev, &sm_count, nullptr, nullptr)) return st;
+  CUtensorMap tmk, tmv;
+  TmaCoords kc{}, vc{};
+  if (int st = build_maps(&q, &tmk, &tmv, &kc, &vc)) return st;
+  DecodeArgs a = make_args(&q);
+  a.kc = kc;
+  a.vc = vc;
+  a.key_begin = key_begin;
+  a.key_end = key_end;
+  a.num_splits = q.num_splits;
+  a.split_offset = 0;
+  a.splits_total = q.num_splits;
+  a.write_partials = 1;
+  a.partial_o = partial_o;
+  a.partial_ml = partial_ml;
+  const int grid_y = q.batch * q.heads_kv * a.head_chunks;
+  if (grid_y > 65535)
+    return fail(FLB_ERR_UNSUPPORTED, "batch * heads_kv * head chunks = %d exceeds 65535", grid_y);
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  return dispatch(q.dtype, q.head_dim, [&](auto tag, auto dim) {
+    return launch_split<decltype(tag), decltype(dim)::value>(a, tmk, tmv, q.num_splits, grid_y,
+                                                             stream);
+  });
+}
+
+extern "C" int flb_decode_merge(const float* partial_o, const float* partial_ml, int32_t batch,
+                                int32_t heads, int32_t head_dim, int32_t num_splits,
+                                int32_t dtype, void* o, int64_t o_batch_stride,
+                                int64_t o_head_stride, float* lse, flb_stream_t stream_) {
+  clear_error();
+  if (!partial_o || !partial_ml || !o || !lse)
+    return fail(FLB_ERR_INVALID_ARGUMENT, "a required pointer is NULL");
+  if (batch <= 0 || heads <= 0 || num_splits <= 0 || (head_dim != 64 && head_dim != 128))
+    return fail(FLB_ERR_INVALID_ARGUMENT, "bad merge shape");
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (dtype == FLB_BF16)
+    return launch_merge<__nv_bfloat16>(partial_o, partial_ml, batch, heads, head_dim, num_splits,
+                                       o, o_batch_stride, o_head_stride, lse, stream);
+  if (dtype == FLB_FP16)
+    return launch_merge<__half>(partial_o, partial_ml, batch, heads, head_dim, num_splits, o,
+                                o_batch_stride, o_head_stride, lse, stream);
+  return fail(FLB_ERR_UNSUPPORTED, "merge takes bf16 or fp16");
+}

@@ -1,0 +1,48 @@
+// Host-side helpers shared by the C-ABI entry points: error reporting, device queries and TMA
+// tensor-map encoding for strided [B, S, H, D] views.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "flash_lab_b200.h"
+
+namespace flb {
+
+// Records a printf-style message for flb_last_error() on this thread and returns `status`.
+int fail(int status, const char* fmt, ...);
+void clear_error();
+const char* g_last_error_message();
+
+// Returns FLB_OK or FLB_ERR_CUDA with the runtime's message recorded.
+int check_cuda(cudaError_t err, const char* what);
+
+// SM count and compute capability of the current device (cached per device).
+int current_device_info(int* device, int* sm_count, int* cc_major, int* cc_minor);
+
+// A [B, S, H, D] tensor view with element strides (the D stride must be 1).
+struct View4 {
+  const void* base;
+  int64_t size[4];    // B, S, H, D
+  int64_t stride[4];  // elements
+  int elem_bytes;
+};
+
+// Where each logical coordinate goes in the 4-D TMA coordinate vector (slot 0 is always D).
+struct TmaCoords {
+  int8_t pos_s, pos_h, pos_b, pad;
+};
+
+// Encodes a tiled TMA map over `v` whose box is [box_rows along S] x [64 along D] (one head, one
+// batch), 128-byte swizzled. Outer dimensions are ordered by increasing stride. Returns FLB_OK,
+// FLB_ERR_MISALIGNED or FLB_ERR_CUDA.
+int encode_rows_x64_map(CUtensorMap* map, TmaCoords* coords, const View4& v, int box_rows,
+                        int dtype);
+
+// The 16-byte row rule every kernel here relies on: base pointer and every stride of a dimension
+// longer than 1 are multiples of 16 bytes, and the head_dim stride is 1.
+bool rows_16b_aligned(const View4& v);
+
+}  // namespace flb

@@ -1,0 +1,494 @@
+// Attention forward (prefill) for sm_100a with tcgen05 tensor cores, TMEM accumulators and TMA.
+//
+// Reference behaviour: the FlashAttention-2 forward of tfan2437/flash-attention-lab,
+// csrc/prefill/mma_pipelined.cu:55-149 with the tile math of csrc/prefill/mma_tile.cuh:40-174
+// (bottom-right causal mask, exp2-domain online softmax whose reference point is 0 for rows that
+// have seen only masked keys, natural-log LSE = m * scale + ln l, -inf for rows without keys) and
+// the host glue of csrc/common/attn_host.h:18-93.
+//
+// B200 design (not a port):
+//  * CTA = 256 query rows of one (batch, head) as two 128-row Q tiles; one softmax warpgroup per
+//    Q tile. Warp 8 is the TMA producer, warp 9 issues every tcgen05.mma from one thread.
+//  * Q (once) and 128-key K / V tiles arrive by TMA in 128-byte-swizzled [128 x 64] boxes; K and
+//    V alternate through a 4-slot mbarrier ring.
+//  * TMEM (512 columns): S0 | S1 | O0 | O1, 128 fp32 columns each. S = Q K^T is an SS UMMA
+//    (M=128, N=128, K=16 steps). The softmax warpgroup reads its S row (thread = row = TMEM lane),
+//    writes P as packed 16-bit pairs over the first 64 columns of the same S region, and O += P V
+//    is a TS UMMA with P taken from TMEM and V as an MN-major shared-memory operand.
+//  * The MMA thread interleaves the two Q tiles: PV0(j), S0(j+1), PV1(j), S1(j+1), so one tile's
+//    softmax overlaps the other tile's GEMMs.
+//  * Online softmax in the exp2 domain with a lazily updated reference point: the running max is
+//    only moved (and O, l rescaled in TMEM) when a tile's max exceeds it by more than 2^8, so
+//    probabilities stay <= 256 and the common case never touches O. The final O / l and the LSE
+//    are exact for any reference point.
+//  * Causal CTAs are launched heaviest first; tiles past the diagonal are never loaded, tiles
+//    crossing it are masked element-wise.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <type_traits>
+
+#include "host_common.h"
+#include "sm100.cuh"
+
+namespace flb {
+namespace {
+
+constexpr int kBM = 128;                       // rows per Q tile
+constexpr int kBN = 128;                       // keys per K/V tile
+constexpr int kHeadDim = 128;
+constexpr int kQTiles = 2;                     // Q tiles per CTA
+constexpr int kRowsPerCta = kBM * kQTiles;
+constexpr int kSlots = 4;                      // K/V ring slots
+constexpr int kTileBytes = kBM * kHeadDim * 2; // 32 KB: two [128 x 64] swizzled boxes
+constexpr int kBoxBytes = kTileBytes / 2;
+constexpr int kSmemData = (kQTiles + kSlots) * kTileBytes;
+constexpr int kSmemBytes = kSmemData + 1024 + 256;
+constexpr int kThreads = 320;                  // 2 softmax warpgroups + producer + MMA warp
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr uint32_t kTmemCols = 512;
+constexpr float kRescaleThreshold = 8.0f;      // log2 units: p <= 2^8 between rescales
+
+struct PrefillArgs {
+  void* o;
+  float* lse;
+  int* status;
+  int64_t o_batch_stride, o_seq_stride, o_head_stride;
+  int batch, seqlen_q, seqlen_k, heads, heads_kv, group;
+  int causal, causal_offset;
+  int q_blocks;
+  float scale, scale_log2;
+  TmaCoords qc, kc, vc;
+};
+
+struct SharedBarriers {
+  uint64_t q_full;
+  uint64_t kv_full[kSlots];
+  uint64_t kv_empty[kSlots];
+  uint64_t s_full[kQTiles];
+  uint64_t p_full[kQTiles];
+  uint64_t o_full[kQTiles];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__device__ __forceinline__ int tma_c(const TmaCoords& c, int slot, int s, int h, int b) {
+  return c.pos_s == slot ? s : (c.pos_h == slot ? h : b);
+}
+
+// Loads a [128 rows x 128 dims] tile as two swizzled boxes.
+__device__ __forceinline__ void load_tile(uint8_t* dst, const CUtensorMap* map,
+                                          const TmaCoords& c, uint64_t* bar, int row, int head,
+                                          int b) {
+#pragma unroll
+  for (int box = 0; box < 2; ++box) {
+    tma_load_4d(dst + box * kBoxBytes, map, bar, box * 64, tma_c(c, 1, row, head, b),
+                tma_c(c, 2, row, head, b), tma_c(c, 3, row, head, b));
+  }
+}
+
+// K-major SW128 operand (Q or K tile): k-step kk (16 elements) of a [128 x 128] tile.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile_addr, int kk) {
+  return umma_smem_desc_sw128(tile_addr + (kk >> 2) * kBoxBytes + (kk & 3) * 32, 16, 1024);
+}
+
+// MN-major SW128 operand (V tile, N = head_dim): k-step kk covers keys 16kk..16kk+15.
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile_addr, int kk) {
+  return umma_smem_desc_sw128(tile_addr + kk * 2048, kBoxBytes, 1024);
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 pack8(const float* x, float scale) {
+  uint4 r;
+  r.x = pack2<T>(x[0] * scale, x[1] * scale);
+  r.y = pack2<T>(x[2] * scale, x[3] * scale);
+  r.z = pack2<T>(x[4] * scale, x[5] * scale);
+  r.w = pack2<T>(x[6] * scale, x[7] * scale);
+  return r;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_kernel(const __grid_constant__ PrefillArgs a, const __grid_constant__ CUtensorMap tmq,
+                   const __grid_constant__ CUtensorMap tmk,
+                   const __grid_constant__ CUtensorMap tmv) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* q_smem = smem;                               // kQTiles tiles
+  uint8_t* ring = smem + kQTiles * kTileBytes;          // kSlots tiles
+  SharedBarriers* sb = reinterpret_cast<SharedBarriers*>(smem + kSmemData);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // Work item, heaviest first for causal attention.
+  const int bh_count = a.batch * a.heads;
+  const int bh = blockIdx.x % bh_count;
+  const int rank = blockIdx.x / bh_count;
+  const int qb = a.causal ? (a.q_blocks - 1 - rank) : rank;
+  const int b = bh / a.heads;
+  const int h = bh - b * a.heads;
+  const int hkv = h / a.group;
+  const int q0 = qb * kRowsPerCta;
+
+  const int kv_tiles_all = (a.seqlen_k + kBN - 1) / kBN;
+  int n_kv = kv_tiles_all;
+  if (a.causal) {
+    const int last_row = min(q0 + kRowsPerCta, a.seqlen_q) - 1;
+    const int max_key = last_row + a.causal_offset;  // last key any row of the CTA sees
+    n_kv = max_key < 0 ? 0 : min(kv_tiles_all, max_key / kBN + 1);
+  }
+
+  if (threadIdx.x == 0) {
+    sb->abort_flag = 0;
+    mbar_init(&sb->q_full, 1);
+    for (int i = 0; i < kSlots; ++i) {
+      mbar_init(&sb->kv_full[i], 1);
+      mbar_init(&sb->kv_empty[i], 1);
+    }
+    for (int t = 0; t < kQTiles; ++t) {
+      mbar_init(&sb->s_full[t], 1);
+      mbar_init(&sb->p_full[t], kBM);
+      mbar_init(&sb->o_full[t], 1);
+    }
+    mbar_init(&sb->mma_done, 1);
+    fence_barrier_init();
+  }
+  if (warp == kProducerWarp) {
+    tmem_alloc(&sb->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sb->tmem_base;
+  const WaitGuard guard{reinterpret_cast<volatile int*>(&sb->abort_flag), a.status};
+
+  if (warp == kProducerWarp) {
+    // ------------------------------- TMA producer -------------------------------
+    if (lane == 0 && n_kv > 0) {
+      tma_prefetch_desc(&tmq);
+      tma_prefetch_desc(&tmk);
+      tma_prefetch_desc(&tmv);
+      mbar_arrive_expect_tx(&sb->q_full, kQTiles * kTileBytes);
+      for (int t = 0; t < kQTiles; ++t) {
+        load_tile(q_smem + t * kTileBytes, &tmq, a.qc, &sb->q_full, q0 + t * kBM, h, b);
+      }
+      int issued = 0;
+      bool ok = true;
+      for (int j = 0; j < n_kv && ok; ++j) {
+        for (int kind = 0; kind < 2; ++kind) {
+          const int i = 2 * j + kind;
+          const int slot = i % kSlots;
+          if (i >= kSlots && !mbar_wait(&sb->kv_empty[slot], ((i / kSlots) - 1) & 1, guard)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&sb->kv_full[slot], kTileBytes);
+          load_tile(ring + slot * kTileBytes, kind == 0 ? &tmk : &tmv, kind == 0 ? a.kc : a.vc,
+                    &sb->kv_full[slot], j * kBN, hkv, b);
+          issued = i + 1;
+        }
+      }
+      // Wait for the copies still landing before the CTA may exit.
+      mbar_wait(&sb->q_full, 0, guard);
+      for (int i = issued > kSlots ? issued - kSlots : 0; i < issued; ++i) {
+        if (!mbar_wait(&sb->kv_full[i % kSlots], (i / kSlots) & 1, guard)) break;
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // ------------------------------- MMA issuer -------------------------------
+    if (lane == 0 && n_kv > 0) {
+      constexpr int kFmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+      constexpr uint32_t kIdescQK = umma_idesc_f16(kFmt, kBM, kBN, 0);
+      constexpr uint32_t kIdescPV = umma_idesc_f16(kFmt, kBM, kHeadDim, 1);
+      const uint32_t q_addr = smem_u32(q_smem);
+      const uint32_t ring_addr = smem_u32(ring);
+      bool ok = mbar_wait(&sb->q_full, 0, guard);
+      // S_t(0) for both Q tiles.
+      if (ok) ok = mbar_wait(&sb->kv_full[0], 0, guard);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < kQTiles; ++t) {
+#pragma unroll
+          for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+            umma_ss(tmem + t * 128, kmajor_desc(q_addr + t * kTileBytes, kk),
+                    kmajor_desc(ring_addr, kk), kIdescQK, kk > 0);
+          }
+          umma_commit(&sb->s_full[t]);
+        }
+        umma_commit(&sb->kv_empty[0]);
+      }
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int iv = 2 * j + 1;  // V_j ring index
+        const int sv = iv % kSlots;
+        const int ik = 2 * j + 2;  // K_{j+1} ring index
+        const int sk = ik % kSlots;
+        const bool more = j + 1 < n_kv;
+        if (!mbar_wait(&sb->kv_full[sv], (iv / kSlots) & 1, guard)) break;
+        for (int t = 0; t < kQTiles; ++t) {
+          if (!mbar_wait(&sb->p_full[t], j & 1, guard)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t v_addr = ring_addr + sv * kTileBytes;
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk) {
+            umma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, mnmajor_desc(v_addr, kk), kIdescPV,
+                    (j > 0 || kk > 0) ? 1u : 0u);
+          }
+          if (t == kQTiles - 1) umma_commit(&sb->kv_empty[sv]);
+          if (more) {
+            if (t == 0 && !mbar_wait(&sb->kv_full[sk], (ik / kSlots) & 1, guard)) {
+              ok = false;
+              break;
+            }
+            const uint32_t k_addr = ring_addr + sk * kTileBytes;
+#pragma unroll
+            for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+              umma_ss(tmem + t * 128, kmajor_desc(q_addr + t * kTileBytes, kk), kmajor_desc(k_addr, kk),
+                      kIdescQK, kk > 0);
+            }
+            umma_commit(&sb->s_full[t]);
+            if (t == kQTiles - 1) umma_commit(&sb->kv_empty[sk]);
+          } else {
+            umma_commit(&sb->o_full[t]);
+          }
+        }
+      }
+      // Every MMA this thread issued has completed before TMEM may be released.
+      umma_commit(&sb->mma_done);
+      mbar_wait(&sb->mma_done, 0, guard);
+    }
+  } else {
+    // ------------------------------- softmax warpgroups -------------------------------
+    const int t = warp >> 2;                  // Q tile of this warpgroup
+    const int quarter = warp & 3;             // TMEM lane quarter this warp may access
+    const int row_in_tile = quarter * 32 + lane;
+    const int row = q0 + t * kBM + row_in_tile;
+    const uint32_t lane_field = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t taddr_s = tmem + t * 128 + lane_field;
+    const uint32_t taddr_o = tmem + 256 + t * 128 + lane_field;
+    const float sl2 = a.scale_log2;
+    const int tile_row0 = q0 + t * kBM;       // first row of this Q tile
+
+    float m_ref = -INFINITY;  // log2-domain reference point of this row
+    float l_sum = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!mbar_wait(&sb->s_full[t], j & 1, guard)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t s[128];
+      tmem_ld32(taddr_s + 0, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+      tmem_ld32(taddr_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+      tmem_ld32(taddr_s + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
+      tmem_ld32(taddr_s + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
+      tmem_ld_wait();
+      float* sf = reinterpret_cast<float*>(s);
+
+      const int k0 = j * kBN;
+      const bool tile_needs_mask =
+          (k0 + kBN > a.seqlen_k) || (a.causal && k0 + kBN - 1 > tile_row0 + a.causal_offset);
+      if (tile_needs_mask) {
+        const int limit = min(a.seqlen_k, a.causal ? row + a.causal_offset + 1 : a.seqlen_k);
+        const int visible = limit - k0;  // keys [k0, k0 + visible) are visible to this row
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          if (c >= visible) sf[c] = -INFINITY;
+        }
+      }
+      float mx4[4] = {sf[0], sf[1], sf[2], sf[3]};
+#pragma unroll
+      for (int c = 4; c < 128; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], sf[c]);
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      const float mt = mx == -INFINITY ? -INFINITY : mx * sl2;
+
+      float m_new = m_ref;
+      if (m_ref == -INFINITY || mt > m_ref + kRescaleThreshold) m_new = fmaxf(m_ref, mt);
+      const bool rescale = (m_new != m_ref) && (m_ref != -INFINITY);
+      const float factor = rescale ? ex2(m_ref - m_new) : 1.f;
+      if (rescale) l_sum *= factor;
+      m_ref = m_new;
+      const float ref = m_ref == -INFINITY ? 0.f : m_ref;
+
+      // P over the first 64 columns of this S region (already read into registers), in halves
+      // so only 32 packed registers are live next to the scores.
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const int i = half * 64 + 2 * c;
+          const float p0 = ex2(fmaf(sf[i], sl2, -ref));
+          const float p1 = ex2(fmaf(sf[i + 1], sl2, -ref));
+          ps[c & 3] += p0 + p1;
+          pk[c] = pack2<T>(p0, p1);
+        }
+        tmem_st32(taddr_s + half * 32, pk);
+      }
+      l_sum += (ps[0] + ps[1]) + (ps[2] + ps[3]);
+      if (__any_sync(0xffffffffu, rescale)) {
+        // O holds PV through tile j-1 (its completion is covered by s_full) and PV of tile j is
+        // not issued before p_full: rescale it in place now that the scores are dead.
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t ov[32];
+          tmem_ld32(taddr_o + c * 32, ov);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            ov[e] = __float_as_uint(__uint_as_float(ov[e]) * factor);
+          }
+          tmem_st32(taddr_o + c * 32, ov);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&sb->p_full[t]);
+    }
+
+    // Epilogue: O / l in the input dtype, and the natural-log LSE.
+    if (ok && n_kv > 0) ok = mbar_wait(&sb->o_full[t], 0, guard);
+    if (ok) {
+      tc_fence_after();
+      const bool row_ok = row < a.seqlen_q;
+      const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+      T* orow = static_cast<T*>(a.o) + static_cast<int64_t>(b) * a.o_batch_stride +
+                static_cast<int64_t>(row) * a.o_seq_stride +
+                static_cast<int64_t>(h) * a.o_head_stride;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t ov[32];
+        if (n_kv > 0) {
+          tmem_ld32(taddr_o + c * 32, ov);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] = 0u;
+        }
+        if (row_ok) {
+          const float* of = reinterpret_cast<const float*>(ov);
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) dst[v] = pack8<T>(of + 8 * v, inv);
+        }
+      }
+      if (row_ok) {
+        a.lse[(static_cast<int64_t>(b) * a.heads + h) * a.seqlen_q + row] =
+            l_sum > 0.f ? m_ref * 0.69314718055994530942f + logf(l_sum) : -INFINITY;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kProducerWarp) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+int validate(const flb_attn_params* p) {
+  if (p == nullptr) return fail(FLB_ERR_INVALID_ARGUMENT, "params is NULL");
+  if (!p->q || !p->k || !p->v || !p->o || !p->lse)
+    return fail(FLB_ERR_INVALID_ARGUMENT, "a required pointer is NULL");
+  if (p->batch <= 0 || p->seqlen_q <= 0 || p->seqlen_k <= 0 || p->heads <= 0 ||
+      p->heads_kv <= 0 || p->head_dim <= 0)
+    return fail(FLB_ERR_INVALID_ARGUMENT, "empty input");
+  if (p->heads % p->heads_kv != 0)
+    return fail(FLB_ERR_INVALID_ARGUMENT,
+                "the number of query heads (%d) must be a multiple of KV heads (%d)", p->heads,
+                p->heads_kv);
+  if (p->dtype != FLB_BF16 && p->dtype != FLB_FP16)
+    return fail(FLB_ERR_UNSUPPORTED, "prefill takes bf16 or fp16 (dtype code %d)", p->dtype);
+  if (p->head_dim != kHeadDim)
+    return fail(FLB_ERR_UNSUPPORTED, "unsupported head_dim %d (this build: 128)", p->head_dim);
+  if (!(p->softmax_scale > 0.f))
+    return fail(FLB_ERR_INVALID_ARGUMENT, "softmax_scale must be positive");
+  const int64_t q_blocks = (p->seqlen_q + kRowsPerCta - 1) / kRowsPerCta;
+  if (q_blocks * p->batch * p->heads > 0x7fffffffLL)
+    return fail(FLB_ERR_UNSUPPORTED, "problem too large for one launch");
+  if (reinterpret_cast<uintptr_t>(p->o) % 16 != 0 ||
+      (p->batch > 1 && (p->o_batch_stride * 2) % 16 != 0) ||
+      (p->seqlen_q > 1 && (p->o_seq_stride * 2) % 16 != 0) ||
+      (p->heads > 1 && (p->o_head_stride * 2) % 16 != 0))
+    return fail(FLB_ERR_MISALIGNED, "o must have 16-byte aligned rows");
+  return FLB_OK;
+}
+
+}  // namespace
+}  // namespace flb
+
+using namespace flb;
+
+extern "C" int flb_prefill_fwd(const flb_attn_params* p, flb_stream_t stream_) {
+  clear_error();
+  if (int st = validate(p)) return st;
+  int dev = 0, sm_count = 0;
+  if (int st = current_device_info(&dev, &sm_count, nullptr, nullptr)) return st;
+
+  View4 qv{p->q, {p->batch, p->seqlen_q, p->heads, p->head_dim},
+           {p->q_batch_stride, p->q_seq_stride, p->q_head_stride, 1}, 2};
+  View4 kv{p->k, {p->batch, p->seqlen_k, p->heads_kv, p->head_dim},
+           {p->k_batch_stride, p->k_seq_stride, p->k_head_stride, 1}, 2};
+  View4 vv{p->v, {p->batch, p->seqlen_k, p->heads_kv, p->head_dim},
+           {p->v_batch_stride, p->v_seq_stride, p->v_head_stride, 1}, 2};
+  CUtensorMap tmq, tmk, tmv;
+  PrefillArgs a{};
+  if (!rows_16b_aligned(qv))
+    return fail(FLB_ERR_MISALIGNED, "q must have 16-byte aligned rows (data pointer and strides)");
+  if (!rows_16b_aligned(kv))
+    return fail(FLB_ERR_MISALIGNED, "k must have 16-byte aligned rows (data pointer and strides)");
+  if (!rows_16b_aligned(vv))
+    return fail(FLB_ERR_MISALIGNED, "v must have 16-byte aligned rows (data pointer and strides)");
+  if (int st = encode_rows_x64_map(&tmq, &a.qc, qv, kBM, p->dtype)) return st;
+  if (int st = encode_rows_x64_map(&tmk, &a.kc, kv, kBN, p->dtype)) return st;
+  if (int st = encode_rows_x64_map(&tmv, &a.vc, vv, kBN, p->dtype)) return st;
+
+  a.o = p->o;
+  a.lse = p->lse;
+  a.status = p->status;
+  a.o_batch_stride = p->o_batch_stride;
+  a.o_seq_stride = p->o_seq_stride;
+  a.o_head_stride = p->o_head_stride;
+  a.batch = p->batch;
+  a.seqlen_q = p->seqlen_q;
+  a.seqlen_k = p->seqlen_k;
+  a.heads = p->heads;
+  a.heads_kv = p->heads_kv;
+  a.group = p->heads / p->heads_kv;
+  a.causal = p->causal ? 1 : 0;
+  a.causal_offset = p->seqlen_k - p->seqlen_q;
+  a.q_blocks = (p->seqlen_q + kRowsPerCta - 1) / kRowsPerCta;
+  a.scale = p->softmax_scale;
+  a.scale_log2 = static_cast<float>(static_cast<double>(p->softmax_scale) * 1.4426950408889634);
+
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  const int grid = a.q_blocks * p->batch * p->heads;
+  auto launch = [&](auto kernel) -> int {
+    static thread_local int configured_device = -1;
+    if (configured_device != dev) {
+      if (int st = check_cuda(
+              cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
+              "cudaFuncSetAttribute(prefill)"))
+        return st;
+      configured_device = dev;
+    }
+    kernel<<<grid, kThreads, kSmemBytes, stream>>>(a, tmq, tmk, tmv);
+    return check_cuda(cudaGetLastError(), "prefill_kernel launch");
+  };
+  if (p->dtype == FLB_BF16) return launch(prefill_kernel<__nv_bfloat16>);
+  return launch(prefill_kernel<__half>);
+}

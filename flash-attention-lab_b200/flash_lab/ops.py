@@ -1,0 +1,363 @@
+"""Public entry points: drop-in for flash_lab/ops.py of tfan2437/flash-attention-lab.
+
+The ops keep the reference's torch.library schemas (csrc/bindings.cpp:12-38 there):
+    flash_lab::attention_<impl>(Tensor q, Tensor k, Tensor v, bool causal, float softmax_scale)
+        -> (Tensor, Tensor)
+    flash_lab::decode_<impl>(Tensor q, Tensor k_cache, Tensor v_cache, Tensor seq_lens,
+        float softmax_scale, int num_splits) -> (Tensor, Tensor)
+with fake (shape-only) kernels, so they trace under torch.compile(fullgraph=True) and replay in
+CUDA graphs. Each op allocates its outputs and workspace with PyTorch's allocator and calls the
+sm_100a library through its C ABI (flash_lab._capi) on the current stream. There is no CPU
+path: without the library, or on a non-CUDA tensor, the ops raise.
+
+Implementations (impl=): "sm100" is the tcgen05 prefill; "mma_pipelined" is kept as a name for
+the same kernel so callers of the reference's op keep working. Decode has "splitkv" (split-KV with
+a fixed-order merge) and "decode_inplace" (one split).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+from dataclasses import dataclass
+
+import torch
+
+from flash_lab import _capi
+from flash_lab.layouts import AttnShape, DecodeShape, check_attention_inputs, check_decode_inputs
+
+try:
+    _LIB = _capi.load()
+except (OSError, AttributeError) as exc:
+    _LIB = None
+    HAS_EXTENSION = False
+    EXTENSION_ERROR = str(exc)
+else:
+    HAS_EXTENSION = True
+    EXTENSION_ERROR = ""
+
+_DTYPE_CODE = {torch.bfloat16: _capi.FLB_BF16, torch.float16: _capi.FLB_FP16}
+DEBUG = os.environ.get("FLASH_LAB_DEBUG", "0") not in ("", "0")
+
+
+@dataclass(frozen=True)
+class PrefillImpl:
+    op: str
+    dtypes: tuple
+    head_dims: tuple
+    gqa: bool = True
+    causal_unequal_lengths: bool = True  # causal with S_q != S_k (bottom-right aligned)
+
+    def unsupported_reason(self, shape: AttnShape, dtype: torch.dtype, causal: bool) -> str | None:
+        if dtype not in self.dtypes:
+            return f"dtype {dtype} is not one of {self.dtypes}"
+        if shape.head_dim not in self.head_dims:
+            return f"head_dim {shape.head_dim} is not one of {self.head_dims}"
+        if shape.group > 1 and not self.gqa:
+            return "grouped-query attention (H_kv < H) is not supported"
+        if causal and shape.seqlen_q != shape.seqlen_k and not self.causal_unequal_lengths:
+            return "causal attention requires S_q == S_k"
+        return None
+
+
+@dataclass(frozen=True)
+class DecodeImpl:
+    op: str
+    dtypes: tuple
+    head_dims: tuple
+    paged: bool = False
+    in_auto: bool = True
+
+    def unsupported_reason(self, shape: DecodeShape, dtype: torch.dtype) -> str | None:
+        if dtype not in self.dtypes:
+            return f"dtype {dtype} is not one of {self.dtypes}"
+        if shape.head_dim not in self.head_dims:
+            return f"head_dim {shape.head_dim} is not one of {self.head_dims}"
+        if shape.paged and not self.paged:
+            return "paged KV caches are not supported"
+        return None
+
+
+_HALF = (torch.bfloat16, torch.float16)
+PREFILL_IMPLS: dict[str, PrefillImpl] = {
+    "sm100": PrefillImpl(op="attention_sm100", dtypes=_HALF, head_dims=(128,)),
+    "mma_pipelined": PrefillImpl(op="attention_mma_pipelined", dtypes=_HALF, head_dims=(128,)),
+}
+DECODE_IMPLS: dict[str, DecodeImpl] = {
+    "splitkv": DecodeImpl(op="decode_splitkv", dtypes=_HALF, head_dims=(64, 128)),
+    "decode_inplace": DecodeImpl(op="decode_inplace", dtypes=_HALF, head_dims=(64, 128)),
+}
+
+_PREFILL_SCHEMA = "(Tensor q, Tensor k, Tensor v, bool causal, float softmax_scale) -> (Tensor, Tensor)"
+_DECODE_SCHEMA = ("(Tensor q, Tensor k_cache, Tensor v_cache, Tensor seq_lens, float softmax_scale,"
+                  " int num_splits) -> (Tensor, Tensor)")
+
+
+# ------------------------------------------------------------------------------------------------
+# Plumbing shared by the op implementations
+# ------------------------------------------------------------------------------------------------
+
+_status_words: dict[int, torch.Tensor] = {}
+_sm_counts: dict[int, int] = {}
+
+
+def _status_ptr(device: torch.device) -> int:
+    """Device status word the kernels raise on a timed-out pipeline wait (0 = healthy)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    word = _status_words.get(idx)
+    if word is None:
+        if torch.cuda.is_current_stream_capturing():
+            return 0
+        word = torch.zeros(1, dtype=torch.int32, device=device)
+        _status_words[idx] = word
+    return word.data_ptr()
+
+
+def device_status(device: torch.device | int | None = None) -> int:
+    """Reads (and clears) the status word of a device: 0, or the code of a timed-out wait."""
+    if device is None:
+        idx = torch.cuda.current_device()
+    elif isinstance(device, int):
+        idx = device
+    else:
+        idx = torch.device(device).index
+        idx = torch.cuda.current_device() if idx is None else idx
+    word = _status_words.get(idx)
+    if word is None:
+        return 0
+    value = int(word.item())
+    word.zero_()
+    return value
+
+
+def _sm_count(device: torch.device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    n = _sm_counts.get(idx)
+    if n is None:
+        n = torch.cuda.get_device_properties(idx).multi_processor_count
+        _sm_counts[idx] = n
+    return n
+
+
+def _require_library() -> ctypes.CDLL:
+    if _LIB is None:
+        raise RuntimeError(f"the sm_100a library did not load: {EXTENSION_ERROR}")
+    return _LIB
+
+
+def _check(status: int, what: str, device: torch.device) -> None:
+    if status != _capi.FLB_OK:
+        raise RuntimeError(f"{what}: {_capi.error_message(_LIB, status)}")
+    if DEBUG:
+        torch.cuda.synchronize(device)
+        code = device_status(device)
+        if code:
+            raise RuntimeError(f"{what}: a kernel pipeline wait timed out (status {code})")
+
+
+class _DeviceGuard:
+    """Makes `device` current for the C-ABI call when it is not already."""
+
+    def __init__(self, device: torch.device):
+        self.idx = device.index
+        self.prev = None
+
+    def __enter__(self):
+        if self.idx is not None:
+            cur = torch.cuda.current_device()
+            if cur != self.idx:
+                self.prev = cur
+                torch.cuda.set_device(self.idx)
+
+    def __exit__(self, *exc):
+        if self.prev is not None:
+            torch.cuda.set_device(self.prev)
+
+
+# ------------------------------------------------------------------------------------------------
+# Op implementations (CUDA dispatch key)
+# ------------------------------------------------------------------------------------------------
+
+def _prefill(q, k, v, causal: bool, softmax_scale: float):
+    lib = _require_library()
+    if q.dtype not in _DTYPE_CODE or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise RuntimeError(f"prefill takes bf16 or fp16 tensors of one dtype, got {q.dtype}")
+    batch, seqlen_q, heads, head_dim = q.shape
+    seqlen_k, heads_kv = k.shape[1], k.shape[2]
+    o = torch.empty((batch, seqlen_q, heads, head_dim), dtype=q.dtype, device=q.device)
+    lse = torch.empty((batch, heads, seqlen_q), dtype=torch.float32, device=q.device)
+    p = _capi.AttnParams(
+        q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr(),
+        q.stride(0), q.stride(1), q.stride(2),
+        k.stride(0), k.stride(1), k.stride(2),
+        v.stride(0), v.stride(1), v.stride(2),
+        o.stride(0), o.stride(1), o.stride(2),
+        batch, seqlen_q, seqlen_k, heads, heads_kv, head_dim,
+        1 if causal else 0, _DTYPE_CODE[q.dtype], float(softmax_scale),
+        _status_ptr(q.device),
+    )
+    if q.stride(-1) != 1 or k.stride(-1) != 1 or v.stride(-1) != 1:
+        raise RuntimeError("q, k, v must be contiguous in head_dim")
+    with _DeviceGuard(q.device):
+        status = lib.flb_prefill_fwd(ctypes.byref(p), torch.cuda.current_stream(q.device).cuda_stream)
+    _check(status, "flb_prefill_fwd", q.device)
+    return o, lse
+
+
+def _decode(q, k_cache, v_cache, seq_lens, softmax_scale: float, num_splits: int,
+            allow_splits: bool):
+    lib = _require_library()
+    if q.dtype not in _DTYPE_CODE:
+        raise RuntimeError(f"decode takes bf16 or fp16, got {q.dtype}")
+    if q.dim() != 3 or k_cache.dim() != 4:
+        raise RuntimeError("q must be [B, H, D], caches [B, S_max, H_kv, D]")
+    if seq_lens.dtype != torch.int32 or not seq_lens.is_contiguous():
+        raise RuntimeError("seq_lens must be contiguous int32")
+    batch, heads, head_dim = q.shape
+    max_seqlen, heads_kv = k_cache.shape[1], k_cache.shape[2]
+    if not allow_splits:
+        splits = 1
+    elif num_splits > 0:
+        splits = int(num_splits)
+    else:
+        splits = lib.flb_decode_num_splits(batch, heads, heads_kv, head_dim, max_seqlen,
+                                           _sm_count(q.device))
+    ws_bytes = lib.flb_decode_workspace_bytes(batch, heads, head_dim, splits)
+    workspace = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
+    o = torch.empty((batch, heads, head_dim), dtype=q.dtype, device=q.device)
+    lse = torch.empty((batch, heads), dtype=torch.float32, device=q.device)
+    p = _capi.DecodeParams(
+        q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), o.data_ptr(), lse.data_ptr(),
+        seq_lens.data_ptr(),
+        q.stride(0), q.stride(1),
+        k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
+        v_cache.stride(0), v_cache.stride(1), v_cache.stride(2),
+        o.stride(0), o.stride(1),
+        batch, heads, heads_kv, head_dim, max_seqlen, splits, _DTYPE_CODE[q.dtype],
+        float(softmax_scale),
+        0 if workspace is None else workspace.data_ptr(), ws_bytes,
+        _status_ptr(q.device),
+    )
+    with _DeviceGuard(q.device):
+        status = lib.flb_decode_fwd(ctypes.byref(p), torch.cuda.current_stream(q.device).cuda_stream)
+    _check(status, "flb_decode_fwd", q.device)
+    return o, lse
+
+
+def _prefill_fake(q, k, v, causal, softmax_scale):
+    batch, seqlen_q, heads, _ = q.shape
+    return q.new_empty(q.shape), q.new_empty((batch, heads, seqlen_q), dtype=torch.float32)
+
+
+def _decode_fake(q, k_cache, v_cache, seq_lens, softmax_scale, num_splits):
+    return q.new_empty(q.shape), q.new_empty(q.shape[:2], dtype=torch.float32)
+
+
+_LIBRARIES: list = []  # keeps the torch.library fragments alive
+
+
+def _define(name: str, schema: str, impl, fake) -> None:
+    if hasattr(torch.ops.flash_lab, name):
+        return
+    lib = torch.library.Library("flash_lab", "FRAGMENT")
+    lib.define(name + schema)
+    lib.impl(name, impl, "CUDA")
+    _LIBRARIES.append(lib)
+    torch.library.register_fake(f"flash_lab::{name}", fake, lib=lib)
+
+
+def _register_ops() -> None:
+    for spec in PREFILL_IMPLS.values():
+        _define(spec.op, _PREFILL_SCHEMA, _prefill, _prefill_fake)
+    _define("decode_splitkv", _DECODE_SCHEMA,
+            lambda q, kc, vc, sl, scale, ns: _decode(q, kc, vc, sl, scale, ns, True), _decode_fake)
+    _define("decode_inplace", _DECODE_SCHEMA,
+            lambda q, kc, vc, sl, scale, ns: _decode(q, kc, vc, sl, scale, ns, False),
+            _decode_fake)
+
+
+if HAS_EXTENSION:
+    _register_ops()
+
+_BUILT_OPS = frozenset(
+    spec.op for spec in (*PREFILL_IMPLS.values(), *DECODE_IMPLS.values())
+    if HAS_EXTENSION and hasattr(torch.ops.flash_lab, spec.op)
+)
+
+
+def available_impls() -> dict[str, list[str]]:
+    """Implementations compiled into this build, by entry point."""
+    return {
+        "attention": [name for name, spec in PREFILL_IMPLS.items() if spec.op in _BUILT_OPS],
+        "decode": [name for name, spec in DECODE_IMPLS.items() if spec.op in _BUILT_OPS],
+    }
+
+
+def _select(table: dict, impl: str, device: torch.device, describe, reason_of):
+    """The implementation to run (same rules and messages as the reference's ops.py:139-159)."""
+    if impl != "auto" and impl not in table:
+        raise ValueError(f"unknown impl {impl!r}; choose from {['auto', *table]}")
+    if device.type != "cuda":
+        raise ValueError(f"flash_lab kernels take CUDA tensors, got device {device}")
+    missing = "" if HAS_EXTENSION else f" (the CUDA extension did not load: {EXTENSION_ERROR})"
+    if impl != "auto":
+        spec = table[impl]
+        reason = reason_of(spec)
+        if reason is not None:
+            raise ValueError(f"impl {impl!r} cannot run {describe()}: {reason}")
+        if spec.op not in _BUILT_OPS:
+            raise RuntimeError(f"impl {impl!r} is not available in this build{missing}")
+        return spec
+    for spec in table.values():
+        if getattr(spec, "in_auto", True) and spec.op in _BUILT_OPS and reason_of(spec) is None:
+            return spec
+    raise ValueError(f"no available implementation supports {describe()}{missing}")
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
+              softmax_scale: float | None = None, impl: str = "auto", return_lse: bool = False):
+    """Attention forward. q is [B, S_q, H, D]; k and v are [B, S_k, H_kv, D] with H % H_kv == 0.
+
+    Returns o [B, S_q, H, D] in the input dtype and, with return_lse=True, the natural-log
+    log-sum-exp of each score row as fp32 [B, H, S_q]. Causal masking with S_q != S_k is
+    aligned to the bottom-right corner.
+    """
+    shape = check_attention_inputs(q, k, v)
+    scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(shape.head_dim)
+    if not scale > 0:
+        raise ValueError(f"softmax_scale must be positive, got {scale}")
+    spec = _select(
+        PREFILL_IMPLS, impl, q.device,
+        lambda: (f"dtype={q.dtype}, head_dim={shape.head_dim}, heads={shape.heads}/"
+                 f"{shape.heads_kv}, S_q={shape.seqlen_q}, S_k={shape.seqlen_k}, causal={causal}"),
+        lambda s: s.unsupported_reason(shape, q.dtype, causal),
+    )
+    out, lse = getattr(torch.ops.flash_lab, spec.op)(q, k, v, causal, scale)
+    return (out, lse) if return_lse else out
+
+
+def decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, seq_lens: torch.Tensor,
+           block_tables: torch.Tensor | None = None, softmax_scale: float | None = None,
+           impl: str = "auto", num_splits: int | None = None, return_lse: bool = False):
+    """One decode step: each sequence's single query token attends to its first seq_lens[b] keys.
+
+    The cache is [B, S_max, H_kv, D], read in place through its strides. seq_lens values are not
+    checked on the host (that would force a device sync); the kernel clamps them to [0, S_max].
+    num_splits=None lets the library choose the split count from the shapes only.
+    """
+    q3, shape = check_decode_inputs(q, k_cache, v_cache, seq_lens, block_tables)
+    scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(shape.head_dim)
+    if num_splits is not None and num_splits < 1:
+        raise ValueError(f"num_splits must be positive, got {num_splits}")
+    spec = _select(
+        DECODE_IMPLS, impl, q.device,
+        lambda: (f"dtype={q.dtype}, head_dim={shape.head_dim}, heads={shape.heads}/"
+                 f"{shape.heads_kv}, paged={shape.paged}"),
+        lambda s: s.unsupported_reason(shape, q.dtype),
+    )
+    out, lse = getattr(torch.ops.flash_lab, spec.op)(q3, k_cache, v_cache, seq_lens, scale,
+                                                     num_splits or 0)
+    if q.dim() == 4:
+        out = out.unsqueeze(1)
+    return (out, lse) if return_lse else out

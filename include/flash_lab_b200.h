@@ -1,0 +1,172 @@
+/*
+ * flash_lab_b200.h — C ABI of the B200 (sm_100a) attention library behind flash_lab's operators.
+ *
+ * This ABI replaces the reference's PyTorch-extension boundary (tfan2437/flash-attention-lab):
+ * the op schemas of csrc/bindings.cpp:7-42 and the per-op host glue that checked inputs, built
+ * parameter structs and launched kernels (csrc/common/attn_host.h:18-93,
+ * csrc/prefill/mma_pipelined.cu:152-185, csrc/decode/decode_host.h:18-85,
+ * csrc/decode/decode.cu:231-340). Python binds it with ctypes and registers the same
+ * torch.library schemas on top (flash_lab/_capi.py and flash_lab/ops.py in this repository).
+ *
+ * Conventions
+ *  - Plain C: raw device pointers, int64 element strides, int32 sizes. No torch types.
+ *  - The caller owns every buffer (inputs, outputs, workspaces). Apart from the one entry point
+ *    documented as allocation-free with static scratch, the library allocates nothing, never
+ *    synchronises, and launches only on the stream it is given.
+ *  - Every entry point returns an flb_status. Nothing throws or aborts across the ABI.
+ *    flb_last_error() gives a message for the calling thread's most recent failure.
+ *  - Reentrant: no mutable global state except one-time per-device kernel attribute set-up.
+ *  - Optional `status` device word: kernels whose pipeline waits exceed their deadline write a
+ *    nonzero code there (first writer wins) and return early instead of hanging. Pass NULL to
+ *    skip.
+ */
+#ifndef FLASH_LAB_B200_H_
+#define FLASH_LAB_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FLB_ABI_VERSION 1
+
+/* Stream handle: the same object as cudaStream_t / CUstream (NULL = legacy default stream). */
+typedef struct CUstream_st* flb_stream_t;
+
+typedef enum {
+  FLB_OK = 0,
+  FLB_ERR_INVALID_ARGUMENT = 1, /* null pointer, non-positive size, inconsistent shape */
+  FLB_ERR_UNSUPPORTED = 2,      /* dtype / head_dim / group not compiled into this library */
+  FLB_ERR_MISALIGNED = 3,       /* a pointer or stride breaks the 16-byte row rule */
+  FLB_ERR_CUDA = 4,             /* CUDA runtime or driver error (see flb_last_error) */
+  FLB_ERR_WORKSPACE = 5,        /* workspace missing or smaller than flb_decode_workspace_bytes */
+  FLB_ERR_NO_DEVICE = 6         /* no sm_100 device current */
+} flb_status;
+
+typedef enum { FLB_BF16 = 0, FLB_FP16 = 1 } flb_dtype;
+
+/*
+ * Prefill problem. Mirrors AttnParams (csrc/common/params.h:9-27 of the reference).
+ * q [B, S_q, H, D], k and v [B, S_k, H_kv, D], o [B, S_q, H, D] (input dtype), lse [B, H, S_q]
+ * fp32 contiguous (natural-log log-sum-exp of each scaled score row, -inf for rows that see no
+ * key). Strides are in elements; the head_dim stride must be 1, every other stride and every
+ * base pointer a multiple of 16 bytes. Query head h reads KV head h / (H / H_kv).
+ * Causal masking is aligned to the bottom-right corner: query i sees key j iff
+ * j <= i + (S_k - S_q).
+ */
+typedef struct {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  float* lse;
+  int64_t q_batch_stride, q_seq_stride, q_head_stride;
+  int64_t k_batch_stride, k_seq_stride, k_head_stride;
+  int64_t v_batch_stride, v_seq_stride, v_head_stride;
+  int64_t o_batch_stride, o_seq_stride, o_head_stride;
+  int32_t batch, seqlen_q, seqlen_k, heads, heads_kv, head_dim;
+  int32_t causal;        /* 0 or 1 */
+  int32_t dtype;         /* flb_dtype */
+  float softmax_scale;   /* > 0 */
+  int32_t* status;       /* optional device status word */
+} flb_attn_params;
+
+/*
+ * Decode problem (one query token per sequence). Mirrors DecodeParams
+ * (csrc/common/params.h:31-53 of the reference).
+ * q [B, H, D]; k_cache / v_cache [B, S_max, H_kv, D] read in place through their strides;
+ * seq_lens [B] int32 on the device (values are clamped to [0, S_max] on the device, never read
+ * on the host); o [B, H, D]; lse [B, H] fp32 contiguous.
+ * num_splits: 0 lets the library choose from the shapes only (flb_decode_num_splits), which keeps
+ * the call CUDA-graph safe; 1 runs without a merge step. workspace must hold
+ * flb_decode_workspace_bytes(...) bytes of device memory when the split count is above 1.
+ */
+typedef struct {
+  const void* q;
+  const void* k_cache;
+  const void* v_cache;
+  void* o;
+  float* lse;
+  const int32_t* seq_lens;
+  int64_t q_batch_stride, q_head_stride;
+  int64_t k_batch_stride, k_seq_stride, k_head_stride;
+  int64_t v_batch_stride, v_seq_stride, v_head_stride;
+  int64_t o_batch_stride, o_head_stride;
+  int32_t batch, heads, heads_kv, head_dim, max_seqlen;
+  int32_t num_splits;    /* 0 = choose */
+  int32_t dtype;         /* flb_dtype */
+  float softmax_scale;   /* > 0 */
+  void* workspace;
+  size_t workspace_bytes;
+  int32_t* status;       /* optional device status word */
+} flb_decode_params;
+
+/* ABI version (FLB_ABI_VERSION). No reference counterpart. */
+int flb_version(void);
+
+/* Static text for a status code. No reference counterpart (the reference raised c10 errors,
+ * csrc/common/checks.h:6-25). */
+const char* flb_status_string(int status);
+
+/* Message describing the calling thread's most recent failure ("" if none). */
+const char* flb_last_error(void);
+
+/* Prefill forward: o, lse = attention(q, k, v). Replaces the attention_mma_pipelined op
+ * (csrc/prefill/mma_pipelined.cu:162-185, schema csrc/bindings.cpp:20-21) and its launcher
+ * (mma_pipelined.cu:152-158). bf16 or fp16, head_dim 128. */
+int flb_prefill_fwd(const flb_attn_params* params, flb_stream_t stream);
+
+/* Split count the decode picks when num_splits == 0, from shapes and the SM count only.
+ * Replaces choose_num_splits (csrc/decode/decode.cu:272-280). */
+int flb_decode_num_splits(int32_t batch, int32_t heads, int32_t heads_kv, int32_t head_dim,
+                          int32_t max_seqlen, int32_t sm_count);
+
+/* Bytes of device workspace flb_decode_fwd needs for this split count (0 when num_splits <= 1).
+ * Replaces the per-call partial_o / partial_ml allocations (csrc/decode/decode.cu:303-311). */
+size_t flb_decode_workspace_bytes(int32_t batch, int32_t heads, int32_t head_dim,
+                                  int32_t num_splits);
+
+/* Split-KV decode step. Replaces the decode_splitkv / decode_inplace ops
+ * (csrc/decode/decode.cu:282-340, schemas csrc/bindings.cpp:30-37). bf16 or fp16, head_dim 64
+ * or 128. */
+int flb_decode_fwd(const flb_decode_params* params, flb_stream_t stream);
+
+/*
+ * Raw split partials for a cross-GPU merge: runs the decode kernel on this device's keys
+ * [key_begin, key_end) of every sequence (clamped to its length), cut into `num_splits` ranges
+ * of the same rounding as flb_decode_fwd, and writes
+ *   partial_o  [B, H, num_splits, D] fp32  unnormalised sum_j 2^(s_j - m) v_j
+ *   partial_ml [B, H, num_splits, 2] fp32  (m, l), m the log2-domain reference (-inf if empty)
+ * No counterpart in the reference (single GPU); it generalises the split stage of
+ * csrc/decode/decode.cu:41-202.
+ */
+int flb_decode_partials(const flb_decode_params* params, int32_t key_begin, int32_t key_end,
+                        float* partial_o, float* partial_ml, flb_stream_t stream);
+
+/*
+ * Fixed-order log-sum-exp merge of `num_splits` partials per (b, h) laid out as above (the
+ * global split order is the index order), writing o [B, H, D] (dtype) and lse [B, H].
+ * Replaces merge_kernel (csrc/decode/decode.cu:204-228).
+ */
+int flb_decode_merge(const float* partial_o, const float* partial_ml, int32_t batch,
+                     int32_t heads, int32_t head_dim, int32_t num_splits, int32_t dtype, void* o,
+                     int64_t o_batch_stride, int64_t o_head_stride, float* lse,
+                     flb_stream_t stream);
+
+/*
+ * Unit test of the tcgen05 building blocks the prefill kernel uses (no reference counterpart;
+ * the reference's equivalent is its mma.sync fragment test, csrc/prefill/mma_tile_test.cu).
+ * a [128, 128], b [128, 128] and v [128, 128] bf16 row-major, p [128, 128] bf16 row-major.
+ * Writes s = a b^T (fp32, through TMA + SW128 descriptors + TMEM) and o = p v (fp32, with p
+ * staged in TMEM as the A operand and v as an MN-major B operand).
+ */
+int flb_selftest_umma(const void* a, const void* b, const void* p, const void* v, float* s_out,
+                      float* o_out, int32_t* status, flb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASH_LAB_B200_H_ */

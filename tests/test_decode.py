@@ -1,0 +1,208 @@
+"""The split-KV decode kernel through flash_lab.decode (and so the C ABI) against the numpy oracle
+and the reference's golden vectors. Cases follow the reference's tests/test_decode.py: ragged
+lengths, length 1, GQA groups 4 and 8, random lengths, split counts with empty splits, strided
+caches, rank-3 queries, determinism, rejections; plus poisoned unused cache rows, lengths outside
+[1, S_max] (clamped on the device) and the BASELINE 32K configurations checked on slices."""
+
+import numpy as np
+import pytest
+import torch
+
+import flash_lab
+import oracle
+from checks import check_decode, host64
+from golden_io import bf16_to_f32, load, names
+
+pytestmark = pytest.mark.gpu
+
+IMPLS = ["decode_inplace", "splitkv"]
+DTYPES = [torch.bfloat16, torch.float16]
+
+CASES = [
+    # batch, heads, heads_kv, max_seqlen, head_dim, seq_lens
+    (1, 8, 8, 64, 64, [64]),
+    (4, 8, 1, 1100, 128, [1, 5, 1023, 1100]),
+    (3, 32, 4, 4097, 128, [4097, 64, 1024]),
+    (2, 6, 2, 300, 64, [300, 17]),
+    (2, 32, 8, 700, 128, [700, 333]),
+    (16, 8, 2, 512, 64, "random"),
+    (2, 64, 2, 400, 128, [400, 399]),   # group 32: two head chunks per KV head
+]
+
+
+def make_case(case, dtype, gen):
+    batch, heads, heads_kv, max_seqlen, head_dim, lens = case
+    q = torch.randn(batch, 1, heads, head_dim, device="cuda", dtype=dtype, generator=gen)
+    shape = (batch, max_seqlen, heads_kv, head_dim)
+    k_cache = torch.randn(shape, device="cuda", dtype=dtype, generator=gen)
+    v_cache = torch.randn(shape, device="cuda", dtype=dtype, generator=gen)
+    if lens == "random":
+        seq_lens = torch.randint(1, max_seqlen + 1, (batch,), device="cuda", generator=gen)
+    else:
+        seq_lens = torch.tensor(lens, device="cuda")
+    return q, k_cache, v_cache, seq_lens.to(torch.int32)
+
+
+def case_id(c):
+    return f"B{c[0]}-H{c[1]}-Hkv{c[2]}-S{c[3]}-D{c[4]}"
+
+
+@pytest.mark.parametrize("case", CASES, ids=case_id)
+@pytest.mark.parametrize("dtype", DTYPES, ids=lambda d: str(d).removeprefix("torch."))
+@pytest.mark.parametrize("impl", IMPLS)
+def test_matches_oracle(impl, dtype, case):
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    q, k_cache, v_cache, seq_lens = make_case(case, dtype, gen)
+    out, lse = flash_lab.decode(q, k_cache, v_cache, seq_lens, impl=impl, return_lse=True)
+    check_decode(out, lse, q, k_cache, v_cache, seq_lens)
+
+
+@pytest.mark.parametrize("name", names("decode"))
+def test_matches_reference_goldens(name):
+    g = load(name)
+    q = torch.from_numpy(bf16_to_f32(g["q"])).to("cuda", torch.bfloat16)
+    kc = torch.from_numpy(bf16_to_f32(g["k_cache"])).to("cuda", torch.bfloat16)
+    vc = torch.from_numpy(bf16_to_f32(g["v_cache"])).to("cuda", torch.bfloat16)
+    lens = torch.from_numpy(g["seq_lens"]).to("cuda")
+    for impl in IMPLS:
+        out, lse = flash_lab.decode(q, kc, vc, lens, impl=impl, return_lse=True)
+        ref = g["o"]
+        err = np.abs(host64(out) - ref).max()
+        rounding = np.abs(torch.from_numpy(ref).to(torch.bfloat16).double().numpy() - ref).max()
+        assert err <= 2 * rounding, (name, impl, err, rounding)
+        assert np.abs(host64(lse) - g["lse"]).max() < 1e-3
+
+
+@pytest.mark.parametrize("num_splits", [1, 2, 8, 64, None])
+def test_split_counts(num_splits):
+    # More splits than tiles leaves some splits empty; they must not disturb the merge.
+    gen = torch.Generator(device="cuda").manual_seed(1)
+    q, k_cache, v_cache, seq_lens = make_case((3, 16, 4, 2000, 128, [2000, 40, 777]),
+                                              torch.bfloat16, gen)
+    out, lse = flash_lab.decode(q, k_cache, v_cache, seq_lens, impl="splitkv",
+                                num_splits=num_splits, return_lse=True)
+    check_decode(out, lse, q, k_cache, v_cache, seq_lens)
+
+
+@pytest.mark.parametrize("impl", IMPLS)
+def test_strided_cache_and_rank3_query(impl):
+    # Caches carved out of a larger allocation (every other KV head), q given as [B, H, D].
+    gen = torch.Generator(device="cuda").manual_seed(2)
+    big = torch.randn(2, 600, 8, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+    k_cache, v_cache = big[:, :, 0::2], big[:, :, 1::2]
+    q = torch.randn(2, 16, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+    seq_lens = torch.tensor([600, 123], device="cuda", dtype=torch.int32)
+    out, lse = flash_lab.decode(q, k_cache, v_cache, seq_lens, impl=impl, return_lse=True)
+    assert out.shape == q.shape
+    check_decode(out, lse, q, k_cache, v_cache, seq_lens)
+
+
+@pytest.mark.parametrize("impl", IMPLS)
+def test_head_major_static_cache_view(impl):
+    # The Hugging Face static cache: [B, H_kv, L, D] storage read as [B, L, H_kv, D].
+    gen = torch.Generator(device="cuda").manual_seed(6)
+    kh = torch.randn(2, 4, 1000, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+    vh = torch.randn(2, 4, 1000, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+    q = torch.randn(2, 1, 16, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+    seq_lens = torch.tensor([1000, 517], device="cuda", dtype=torch.int32)
+    out, lse = flash_lab.decode(q, kh.transpose(1, 2), vh.transpose(1, 2), seq_lens, impl=impl,
+                                return_lse=True)
+    check_decode(out, lse, q, kh.transpose(1, 2), vh.transpose(1, 2), seq_lens)
+
+
+@pytest.mark.parametrize("impl", IMPLS)
+def test_unused_rows_are_never_read(impl):
+    # NaN past each sequence's length must not reach the output (0 * NaN would).
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    q, k_cache, v_cache, seq_lens = make_case((3, 8, 2, 333, 128, [333, 70, 1]), torch.bfloat16,
+                                              gen)
+    for b, n in enumerate(seq_lens.tolist()):
+        k_cache[b, n:] = float("nan")
+        v_cache[b, n:] = float("nan")
+    out, lse = flash_lab.decode(q, k_cache, v_cache, seq_lens, impl=impl, return_lse=True)
+    assert torch.isfinite(out).all()
+    clean_k, clean_v = k_cache.nan_to_num(0.0), v_cache.nan_to_num(0.0)
+    check_decode(out, lse, q, clean_k, clean_v, seq_lens)
+
+
+def test_lengths_outside_the_cache_are_clamped():
+    """seq_lens is never read on the host; the kernel clamps it to [0, S_max]: a length past the
+    cache attends to every row, a length of 0 gives zeros and an LSE of -inf."""
+    gen = torch.Generator(device="cuda").manual_seed(8)
+    q, k_cache, v_cache, _ = make_case((3, 8, 8, 200, 128, [1, 1, 1]), torch.bfloat16, gen)
+    seq_lens = torch.tensor([500, 0, 50], device="cuda", dtype=torch.int32)
+    out, lse = flash_lab.decode(q, k_cache, v_cache, seq_lens, return_lse=True)
+    assert torch.all(out[1] == 0) and torch.isneginf(lse[1]).all()
+    ref, ref_lse = oracle.decode(host64(q[[0, 2]]), host64(k_cache[[0, 2]]),
+                                 host64(v_cache[[0, 2]]), np.array([200, 50]), return_lse=True)
+    assert np.abs(host64(out[[0, 2]]) - ref).max() < 1e-2
+    assert np.abs(host64(lse[[0, 2]]) - ref_lse).max() < 1e-3
+
+
+@pytest.mark.parametrize("impl", IMPLS)
+def test_deterministic(impl):
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    q, k_cache, v_cache, seq_lens = make_case((4, 32, 8, 3000, 128, [3000, 1, 2048, 999]),
+                                              torch.bfloat16, gen)
+    first = flash_lab.decode(q, k_cache, v_cache, seq_lens, impl=impl)
+    second = flash_lab.decode(q, k_cache, v_cache, seq_lens, impl=impl)
+    assert torch.equal(first, second)
+
+
+def test_auto_is_splitkv():
+    gen = torch.Generator(device="cuda").manual_seed(4)
+    q, k_cache, v_cache, seq_lens = make_case((2, 8, 8, 64, 64, [64, 3]), torch.bfloat16, gen)
+    assert torch.equal(flash_lab.decode(q, k_cache, v_cache, seq_lens),
+                       flash_lab.decode(q, k_cache, v_cache, seq_lens, impl="splitkv"))
+
+
+@pytest.mark.parametrize("impl", IMPLS)
+def test_rejects_unsupported(impl):
+    q = torch.randn(1, 1, 4, 96, device="cuda", dtype=torch.bfloat16)
+    cache = torch.randn(1, 8, 4, 96, device="cuda", dtype=torch.bfloat16)
+    seq_lens = torch.tensor([8], device="cuda", dtype=torch.int32)
+    with pytest.raises(ValueError, match="head_dim"):
+        flash_lab.decode(q, cache, cache, seq_lens, impl=impl)
+    q, cache = q[..., :64], torch.randn(4, 4, 4, 64, device="cuda", dtype=torch.bfloat16)
+    tables = torch.zeros(1, 2, device="cuda", dtype=torch.int32)
+    with pytest.raises(ValueError, match="paged"):
+        flash_lab.decode(q.contiguous(), cache, cache, seq_lens, block_tables=tables, impl=impl)
+    q32 = torch.randn(1, 1, 4, 64, device="cuda")
+    c32 = torch.randn(1, 8, 4, 64, device="cuda")
+    with pytest.raises(ValueError, match="dtype"):
+        flash_lab.decode(q32, c32, c32, seq_lens, impl=impl)
+
+
+def _check_slices(out, lse, q, k_cache, v_cache, seq_lens, picks):
+    """Oracle check of selected (b, kv head) slices of a full-size run."""
+    group = q.shape[2] // k_cache.shape[2]
+    for b, hkv in picks:
+        hs = slice(hkv * group, (hkv + 1) * group)
+        n = int(seq_lens[b])
+        ref, ref_lse = oracle.decode(host64(q[b:b + 1, :, hs]),
+                                     host64(k_cache[b:b + 1, :n, hkv:hkv + 1]),
+                                     host64(v_cache[b:b + 1, :n, hkv:hkv + 1]), np.array([n]),
+                                     return_lse=True)
+        err = np.abs(host64(out[b:b + 1, :, hs]) - ref).max()
+        rounding = np.abs(torch.from_numpy(ref).to(torch.bfloat16).double().numpy() - ref).max()
+        assert err <= 2 * rounding, (b, hkv, err, rounding)
+        assert np.abs(host64(lse[b:b + 1, hs]) - ref_lse).max() < 1e-3
+
+
+def test_baseline_mha_32k():
+    """BASELINE decode config: B=8, H=H_kv=32, D=128, S_max=32768, all lengths 32768."""
+    gen = torch.Generator(device="cuda").manual_seed(10)
+    q, k_cache, v_cache, _ = make_case((8, 32, 32, 32768, 128, [1] * 8), torch.bfloat16, gen)
+    seq_lens = torch.full((8,), 32768, device="cuda", dtype=torch.int32)
+    out, lse = flash_lab.decode(q, k_cache, v_cache, seq_lens, return_lse=True)
+    _check_slices(out, lse, q, k_cache, v_cache, seq_lens, [(0, 0), (3, 17), (7, 31)])
+
+
+def test_baseline_gqa_32k_ragged():
+    """BASELINE GQA config: B=8, H=32, H_kv=8, lengths U[16384, 32768] from a seed."""
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    q, k_cache, v_cache, _ = make_case((8, 32, 8, 32768, 128, [1] * 8), torch.bfloat16, gen)
+    seq_lens = torch.randint(16384, 32769, (8,), generator=torch.Generator().manual_seed(0))
+    seq_lens = seq_lens.to("cuda", torch.int32)
+    out, lse = flash_lab.decode(q, k_cache, v_cache, seq_lens, return_lse=True)
+    _check_slices(out, lse, q, k_cache, v_cache, seq_lens, [(0, 0), (4, 5), (7, 7)])
