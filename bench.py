@@ -45,7 +45,8 @@ sys.path.insert(0, str(ROOT))
 
 PREFILL = dict(batch=4, heads=32, heads_kv=32, seqlen=4096, head_dim=128)
 METRIC = "prefill TFLOP/s @(4,32,32,4096,128) bf16; decode HBM GB/s @32K cache"
-CPU_SAMPLE_ROWS = 256
+CPU_SAMPLE_ROWS = 1536
+REFERENCE_STEP_ROWS = 256
 
 
 def prefill_flops(batch, heads, seqlen_q, seqlen_k, head_dim, causal) -> float:
@@ -192,9 +193,9 @@ def run_reference_arm(args) -> None:
         return
     times = []
     for _ in range(max(args.warmup, 0)):
-        cpu_baseline_prefill(rows=32)
+        cpu_baseline_prefill(rows=REFERENCE_STEP_ROWS)
     for _ in range(args.steps):
-        times.append(cpu_baseline_prefill(rows=32))
+        times.append(cpu_baseline_prefill(rows=REFERENCE_STEP_ROWS))
     value = statistics.median(t["value"] for t in times)
     sec = statistics.median(t["seconds"] for t in times)
     b = PREFILL
@@ -206,7 +207,7 @@ def run_reference_arm(args) -> None:
         "ms_per_step": full_ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f64", "data": "synthetic",
         "config": {"workload": "prefill (B,H,H_kv,S,D)=(4,32,32,4096,128) non-causal",
-                   "sample": "32 query rows per step (all 128 (b,h), 4096 keys)",
+                   "sample": f"{REFERENCE_STEP_ROWS} query rows per step (all 128 (b,h), 4096 keys)",
                    "ms_per_step_is": "extrapolated time of one full call at the sampled rate"},
         "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": times[0]["cores"],
                          "kind": "port", "sample": times[0]["sample"] + f"; median {sec:.2f} s"},
@@ -224,7 +225,13 @@ def main() -> int:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-extra", action="store_true", help="skip the secondary configurations")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--profile", default=None,
+                    choices=["prefill", "prefill_causal", "decode_mha", "decode_gqa"],
+                    help="run only warmup + steps launches of one kernel (for ncu captures)")
+    ap.add_argument("--batch", type=int, default=None, help="batch size of --profile")
     args = ap.parse_args()
+    if args.profile is not None:
+        return run_profile_case(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
@@ -390,6 +397,41 @@ def run_extra(torch, flash_lab, device, dist, world, rank, args, peaks, traffic)
                      "l2": "512 MB buffer zeroed before every call (outside the events)"}
         del qd, kc, vc
     return out
+
+
+def run_profile_case(args) -> int:
+    """A few launches of one kernel at a reduced batch, for Nsight Compute captures."""
+    import torch
+
+    import flash_lab
+
+    device = torch.device("cuda", 0)
+    gen = torch.Generator(device=device).manual_seed(0)
+    d = 128
+    if args.profile.startswith("prefill"):
+        b = args.batch or 2
+        s, h = PREFILL["seqlen"], PREFILL["heads"]
+        q = torch.randn(b, s, h, d, device=device, dtype=torch.bfloat16, generator=gen)
+        k = torch.randn(b, s, h, d, device=device, dtype=torch.bfloat16, generator=gen)
+        v = torch.randn(b, s, h, d, device=device, dtype=torch.bfloat16, generator=gen)
+        causal = args.profile == "prefill_causal"
+        fn = lambda: flash_lab.attention(q, k, v, causal=causal)  # noqa: E731
+        what = f"prefill B={b} H=32 S=4096 D=128 causal={causal}"
+    else:
+        b = args.batch or 2
+        hk = 32 if args.profile == "decode_mha" else 8
+        smax = 32768
+        qd = torch.randn(b, 1, 32, d, device=device, dtype=torch.bfloat16, generator=gen)
+        kc = torch.randn(b, smax, hk, d, device=device, dtype=torch.bfloat16, generator=gen)
+        vc = torch.randn(b, smax, hk, d, device=device, dtype=torch.bfloat16, generator=gen)
+        lens = torch.full((b,), smax, device=device, dtype=torch.int32)
+        fn = lambda: flash_lab.decode(qd, kc, vc, lens)  # noqa: E731
+        what = f"decode B={b} H=32 H_kv={hk} S=32768 D=128"
+    for _ in range(args.warmup + args.steps):
+        fn()
+    torch.cuda.synchronize()
+    print(f"profile case done: {what}, {args.warmup + args.steps} calls")
+    return 0
 
 
 if __name__ == "__main__":

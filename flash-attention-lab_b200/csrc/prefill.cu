@@ -400,6 +400,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// One shared-memory opt-in per (kernel instantiation, device) and host thread.
+template <typename T>
+int launch_prefill(const PrefillArgs& a, const CUtensorMap& tmq, const CUtensorMap& tmk,
+                   const CUtensorMap& tmv, int grid, int dev, cudaStream_t stream) {
+  static thread_local int configured_device = -1;
+  if (configured_device != dev) {
+    if (int st = check_cuda(cudaFuncSetAttribute(prefill_kernel<T>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 kSmemBytes),
+                            "cudaFuncSetAttribute(prefill)"))
+      return st;
+    configured_device = dev;
+  }
+  prefill_kernel<T><<<grid, kThreads, kSmemBytes, stream>>>(a, tmq, tmk, tmv);
+  return check_cuda(cudaGetLastError(), "prefill_kernel launch");
+}
+
 int validate(const flb_attn_params* p) {
   if (p == nullptr) return fail(FLB_ERR_INVALID_ARGUMENT, "params is NULL");
   if (!p->q || !p->k || !p->v || !p->o || !p->lse)
@@ -475,20 +492,8 @@ extern "C" int flb_prefill_fwd(const flb_attn_params* p, flb_stream_t stream_) {
   a.scale = p->softmax_scale;
   a.scale_log2 = static_cast<float>(static_cast<double>(p->softmax_scale) * 1.4426950408889634);
 
-  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   const int grid = a.q_blocks * p->batch * p->heads;
-  auto launch = [&](auto kernel) -> int {
-    static thread_local int configured_device = -1;
-    if (configured_device != dev) {
-      if (int st = check_cuda(
-              cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes),
-              "cudaFuncSetAttribute(prefill)"))
-        return st;
-      configured_device = dev;
-    }
-    kernel<<<grid, kThreads, kSmemBytes, stream>>>(a, tmq, tmk, tmv);
-    return check_cuda(cudaGetLastError(), "prefill_kernel launch");
-  };
-  if (p->dtype == FLB_BF16) return launch(prefill_kernel<__nv_bfloat16>);
-  return launch(prefill_kernel<__half>);
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (p->dtype == FLB_BF16) return launch_prefill<__nv_bfloat16>(a, tmq, tmk, tmv, grid, dev, stream);
+  return launch_prefill<__half>(a, tmq, tmk, tmv, grid, dev, stream);
 }

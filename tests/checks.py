@@ -97,8 +97,8 @@ def check_prefill(out, lse, q, k, v, causal, scale=None, rows=None, baseline_rul
     assert np.all(np.isneginf(got_lse[~visible]))
     if visible.any():
         lse_t = host64(torch_lse_at_dtype(q, k, v, rows, causal, scale))
-        lse_err = float(np.abs(got_lse - ref_lse)[visible].max())
-        lse_err_torch = float(np.abs(lse_t - ref_lse)[visible].max())
+        lse_err = float(np.abs(got_lse[visible] - ref_lse[visible]).max())
+        lse_err_torch = float(np.abs(lse_t[visible] - ref_lse[visible]).max())
         info.update(lse_err=lse_err, lse_err_torch=lse_err_torch)
         assert lse_err <= 2 * lse_err_torch + LSE_FLOOR[dtype], info
     return info
