@@ -51,39 +51,44 @@ def needs_rebuild() -> bool:
     return any(p.stat().st_mtime > stamp for p in deps)
 
 
-def compile_one(src: pathlib.Path, debug: bool) -> tuple[pathlib.Path, str]:
-    obj = BUILD / (src.name + ".o")
+def compile_one(src: pathlib.Path, debug: bool, defines=(), build_dir=None):
+    obj = (build_dir or BUILD) / (src.name + ".o")
     cmd = [nvcc(), *ARCH, *COMMON, "-c", str(src), "-o", str(obj)]
     if src.suffix == ".cu":
         cmd += ["-Xptxas", "-v"]
     if debug:
         cmd += ["-DFLB_DEBUG=1"]
+    cmd += [f"-D{d}" for d in defines]
     proc = subprocess.run(cmd, capture_output=True, text=True)
     if proc.returncode != 0:
         raise RuntimeError(f"nvcc failed on {src.name}:\n{proc.stdout}\n{proc.stderr}")
     return obj, proc.stderr
 
 
-def build(force: bool = False, debug: bool = False, verbose: bool = False) -> pathlib.Path:
-    if not force and not needs_rebuild():
+def build(force: bool = False, debug: bool = False, verbose: bool = False, defines=(),
+          out: pathlib.Path | None = None) -> pathlib.Path:
+    """Builds the library (to `out` with extra -D `defines` for instrumented variants)."""
+    lib = out or LIB
+    if not force and out is None and not needs_rebuild():
         return LIB
-    BUILD.mkdir(exist_ok=True)
+    build_dir = BUILD if out is None else pathlib.Path(str(out) + ".build")
+    build_dir.mkdir(exist_ok=True, parents=True)
     srcs = sources()
     with cf.ThreadPoolExecutor(max_workers=min(8, len(srcs))) as pool:
-        results = list(pool.map(lambda s: compile_one(s, debug), srcs))
+        results = list(pool.map(lambda s: compile_one(s, debug, defines, build_dir), srcs))
     report = "\n".join(f"== {src.name}\n{log}" for src, (_, log) in zip(srcs, results))
-    (BUILD / "ptxas.txt").write_text(report)
+    (build_dir / "ptxas.txt").write_text(report)
     if verbose:
         print(report)
-    tmp = LIB.with_suffix(".so.tmp")
+    tmp = lib.with_suffix(".so.tmp")
     # The CUDA runtime is linked statically; driver entry points (cuTensorMapEncodeTiled) are
     # resolved at run time through cudaGetDriverEntryPoint, so the library loads without a GPU.
     cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *[str(o) for o, _ in results]]
     proc = subprocess.run(cmd, capture_output=True, text=True)
     if proc.returncode != 0:
         raise RuntimeError(f"link failed:\n{proc.stdout}\n{proc.stderr}")
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, lib)
+    return lib
 
 
 def main() -> int:
@@ -91,8 +96,12 @@ def main() -> int:
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--debug", action="store_true")
     ap.add_argument("-v", "--verbose", action="store_true")
+    ap.add_argument("-D", dest="defines", action="append", default=[],
+                    help="extra preprocessor define (instrumented builds, e.g. FLB_PREFILL_TRACE)")
+    ap.add_argument("--out", type=pathlib.Path, default=None, help="library path for a variant")
     args = ap.parse_args()
-    lib = build(force=args.force, debug=args.debug, verbose=args.verbose)
+    lib = build(force=args.force, debug=args.debug, verbose=args.verbose, defines=args.defines,
+                out=args.out)
     print(lib)
     return 0
 

@@ -30,10 +30,30 @@
 
 #include <cmath>
 #include <cstdint>
+#include <cstdlib>
 #include <type_traits>
 
 #include "host_common.h"
 #include "sm100.cuh"
+
+
+// Optional phase tracing (build with -DFLB_PREFILL_TRACE): each warp accumulates clock64 cycles
+// per phase and lane 0 of every warp of two CTAs prints them at exit. Off in normal builds.
+#ifdef FLB_PREFILL_TRACE
+#include <cstdio>
+#define FLB_TRACE_DECL unsigned long long tr_[8] = {0, 0, 0, 0, 0, 0, 0, 0}; \
+  unsigned long long tr0_ = clock64(); const unsigned long long trstart_ = tr0_;
+#define FLB_TRACE(i) { const unsigned long long t1_ = clock64(); tr_[i] += t1_ - tr0_; tr0_ = t1_; }
+#define FLB_TRACE_DUMP(role)                                                                  \
+  if ((blockIdx.x == 0 || blockIdx.x == gridDim.x / 2) && lane == 0)                         \
+    printf("trace cta %d warp %d %s total %llu | %llu %llu %llu %llu %llu %llu %llu %llu\n", \
+           blockIdx.x, warp, role, clock64() - trstart_, tr_[0], tr_[1], tr_[2], tr_[3],     \
+           tr_[4], tr_[5], tr_[6], tr_[7]);
+#else
+#define FLB_TRACE_DECL
+#define FLB_TRACE(i)
+#define FLB_TRACE_DUMP(role)
+#endif
 
 namespace flb {
 namespace {
@@ -48,11 +68,22 @@ constexpr int kTileBytes = kBM * kHeadDim * 2; // 32 KB: two [128 x 64] swizzled
 constexpr int kBoxBytes = kTileBytes / 2;
 constexpr int kSmemData = (kQTiles + kSlots) * kTileBytes;
 constexpr int kSmemBytes = kSmemData + 1024 + 256;
-constexpr int kThreads = 320;                  // 2 softmax warpgroups + producer + MMA warp
+// Warps: softmax WG0 (0-3), WG1 (4-7), producer (8), MMA issuer (9). With FLB_PREFILL_REGSPLIT the
+// CTA has 12 warps and setmaxnreg moves registers from warpgroup 2 (producer, MMA, 2 spare) to
+// the softmax warpgroups: launch 168 x 3 warpgroups = 208 + 208 + 80 (+8 spare) per lane.
+#ifdef FLB_PREFILL_REGSPLIT
+constexpr int kThreads = 384;
+#else
+constexpr int kThreads = 320;
+#endif
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
+constexpr int kSoftmaxRegs = 208;
+constexpr int kIssueRegs = 80;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units: p <= 2^8 between rescales
+constexpr int kDefaultPolyPairs = 2;           // of every 8 score pairs, 2^x on the FMA pipe
+constexpr int kDefaultPChunks = 1;             // P published to the MMA warp in this many chunks
 
 struct PrefillArgs {
   void* o;
@@ -71,7 +102,7 @@ struct SharedBarriers {
   uint64_t kv_full[kSlots];
   uint64_t kv_empty[kSlots];
   uint64_t s_full[kQTiles];
-  uint64_t p_full[kQTiles];
+  uint64_t p_half[kQTiles][2];   // P columns 0-31 / 32-63 of a Q tile stored in TMEM
   uint64_t o_full[kQTiles];
   uint64_t mma_done;
   uint32_t tmem_base;
@@ -113,7 +144,45 @@ __device__ __forceinline__ uint4 pack8(const float* x, float scale) {
   return r;
 }
 
-template <typename T>
+// 2^(s * scale_log2 - ref) for one row of 128 scores, row sums in ps, P packed to 16 bits and
+// stored to TMEM columns [0, 64) of the row's S region, published in kChunks chunks (each chunk's
+// barrier completes when all 128 rows stored it). kPoly of every 8 pairs use the FMA-pipe
+// polynomial; the rest use the SFU.
+template <typename T, int kPoly, int kChunks>
+__device__ __forceinline__ void softmax_exp_store(const float* sf, float sl2, float nref,
+                                                  float (&ps)[4], uint32_t taddr_s,
+                                                  uint64_t* chunk_bars) {
+  constexpr int kPairsPerChunk = 64 / kChunks;
+#pragma unroll
+  for (int ch = 0; ch < kChunks; ++ch) {
+#pragma unroll
+    for (int q = 0; q < kPairsPerChunk / 32; ++q) {
+      uint32_t pk[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const int pair = ch * kPairsPerChunk + q * 32 + c;
+        const int i = 2 * pair;
+        float x0, x1, p0, p1;
+        ffma2(x0, x1, sf[i], sf[i + 1], sl2, sl2, nref, nref);
+        if ((pair & 7) < kPoly) {
+          exp2_poly2(p0, p1, x0, x1);
+        } else {
+          p0 = ex2(x0);
+          p1 = ex2(x1);
+        }
+        const int acc = (c & 1) * 2;
+        fadd2(ps[acc], ps[acc + 1], ps[acc], ps[acc + 1], p0, p1);
+        pk[c] = pack2<T>(p0, p1);
+      }
+      tmem_st32(taddr_s + ch * (kPairsPerChunk) + q * 32, pk);
+    }
+    tmem_st_wait();
+    tc_fence_before();
+    mbar_arrive(&chunk_bars[ch]);
+  }
+}
+
+template <typename T, int kPolyPairs, int kPChunks>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ PrefillArgs a, const __grid_constant__ CUtensorMap tmq,
                    const __grid_constant__ CUtensorMap tmk,
@@ -128,11 +197,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Work item, heaviest first for causal attention.
-  const int bh_count = a.batch * a.heads;
-  const int bh = blockIdx.x % bh_count;
-  const int rank = blockIdx.x / bh_count;
-  const int qb = a.causal ? (a.q_blocks - 1 - rank) : rank;
+  // Work item: the q-blocks of one (batch, head) are adjacent in launch order, so the CTAs
+  // running together share their K/V tiles in L2 (heads of one GQA group are adjacent too).
+  // Causal q-blocks run heaviest first within each head, so the last CTAs launched are light.
+  const int bh = blockIdx.x / a.q_blocks;
+  const int qrank = blockIdx.x - bh * a.q_blocks;
+  const int qb = a.causal ? (a.q_blocks - 1 - qrank) : qrank;
   const int b = bh / a.heads;
   const int h = bh - b * a.heads;
   const int hkv = h / a.group;
@@ -155,7 +225,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int t = 0; t < kQTiles; ++t) {
       mbar_init(&sb->s_full[t], 1);
-      mbar_init(&sb->p_full[t], kBM);
+      mbar_init(&sb->p_half[t][0], kBM);
+      mbar_init(&sb->p_half[t][1], kBM);
       mbar_init(&sb->o_full[t], 1);
     }
     mbar_init(&sb->mma_done, 1);
@@ -170,9 +241,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sb->tmem_base;
   const WaitGuard guard{reinterpret_cast<volatile int*>(&sb->abort_flag), a.status};
-
+#ifdef FLB_PREFILL_REGSPLIT
+  if (warp >= kProducerWarp) warpgroup_regs_dec<kIssueRegs>();
+#endif
   if (warp == kProducerWarp) {
     // ------------------------------- TMA producer -------------------------------
+    FLB_TRACE_DECL
     if (lane == 0 && n_kv > 0) {
       tma_prefetch_desc(&tmq);
       tma_prefetch_desc(&tmk);
@@ -187,10 +261,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kind = 0; kind < 2; ++kind) {
           const int i = 2 * j + kind;
           const int slot = i % kSlots;
+          FLB_TRACE(1)
           if (i >= kSlots && !mbar_wait(&sb->kv_empty[slot], ((i / kSlots) - 1) & 1, guard)) {
             ok = false;
             break;
           }
+          FLB_TRACE(0)
           mbar_arrive_expect_tx(&sb->kv_full[slot], kTileBytes);
           load_tile(ring + slot * kTileBytes, kind == 0 ? &tmk : &tmv, kind == 0 ? a.kc : a.vc,
                     &sb->kv_full[slot], j * kBN, hkv, b);
@@ -203,28 +279,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&sb->kv_full[i % kSlots], (i / kSlots) & 1, guard)) break;
       }
     }
+    FLB_TRACE_DUMP("producer(0=wait_empty,1=issue)")
   } else if (warp == kMmaWarp) {
+    FLB_TRACE_DECL
     // ------------------------------- MMA issuer -------------------------------
-    if (lane == 0 && n_kv > 0) {
+    // The whole warp runs this loop (waits and descriptors stay warp-uniform); elect.sync picks
+    // the one lane that issues each tcgen05.mma / commit.
+    FLB_TRACE_DECL
+    if (n_kv > 0) {
       constexpr int kFmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
       constexpr uint32_t kIdescQK = umma_idesc_f16(kFmt, kBM, kBN, 0);
       constexpr uint32_t kIdescPV = umma_idesc_f16(kFmt, kBM, kHeadDim, 1);
       const uint32_t q_addr = smem_u32(q_smem);
       const uint32_t ring_addr = smem_u32(ring);
-      bool ok = mbar_wait(&sb->q_full, 0, guard);
-      // S_t(0) for both Q tiles.
-      if (ok) ok = mbar_wait(&sb->kv_full[0], 0, guard);
+      bool ok = mbar_wait(&sb->q_full, 0, guard) && mbar_wait(&sb->kv_full[0], 0, guard);
+      ok = __all_sync(0xffffffffu, ok);
       if (ok) {
         tc_fence_after();
+#pragma unroll
         for (int t = 0; t < kQTiles; ++t) {
 #pragma unroll
           for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-            umma_ss(tmem + t * 128, kmajor_desc(q_addr + t * kTileBytes, kk),
-                    kmajor_desc(ring_addr, kk), kIdescQK, kk > 0);
+            umma_ss_elect(tmem + t * 128, kmajor_desc(q_addr + t * kTileBytes, kk),
+                          kmajor_desc(ring_addr, kk), kIdescQK, kk > 0);
           }
-          umma_commit(&sb->s_full[t]);
+          umma_commit_elect(&sb->s_full[t]);
         }
-        umma_commit(&sb->kv_empty[0]);
+        umma_commit_elect(&sb->kv_empty[0]);
       }
       for (int j = 0; j < n_kv && ok; ++j) {
         const int iv = 2 * j + 1;  // V_j ring index
@@ -232,44 +313,60 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ik = 2 * j + 2;  // K_{j+1} ring index
         const int sk = ik % kSlots;
         const bool more = j + 1 < n_kv;
-        if (!mbar_wait(&sb->kv_full[sv], (iv / kSlots) & 1, guard)) break;
-        for (int t = 0; t < kQTiles; ++t) {
-          if (!mbar_wait(&sb->p_full[t], j & 1, guard)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t v_addr = ring_addr + sv * kTileBytes;
+        FLB_TRACE(2)
+        ok = __all_sync(0xffffffffu, mbar_wait(&sb->kv_full[sv], (iv / kSlots) & 1, guard));
+        if (!ok) break;
+        FLB_TRACE(0)
+        const uint32_t v_addr = ring_addr + sv * kTileBytes;
+        const uint32_t k_addr = ring_addr + sk * kTileBytes;
 #pragma unroll
-          for (int kk = 0; kk < kBN / 16; ++kk) {
-            umma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, mnmajor_desc(v_addr, kk), kIdescPV,
-                    (j > 0 || kk > 0) ? 1u : 0u);
-          }
-          if (t == kQTiles - 1) umma_commit(&sb->kv_empty[sv]);
-          if (more) {
-            if (t == 0 && !mbar_wait(&sb->kv_full[sk], (ik / kSlots) & 1, guard)) {
-              ok = false;
-              break;
+        for (int t = 0; t < kQTiles; ++t) {
+          // P arrives in kPChunks chunks of keys; each chunk's k-steps are issued as soon as
+          // the softmax warpgroup has stored it.
+#pragma unroll
+          for (int ch = 0; ch < kPChunks; ++ch) {
+            ok = __all_sync(0xffffffffu, mbar_wait(&sb->p_half[t][ch], j & 1, guard));
+            if (!ok) break;
+            FLB_TRACE(1)
+            tc_fence_after();
+#pragma unroll
+            for (int kq = 0; kq < kBN / 16 / kPChunks; ++kq) {
+              const int kk = ch * (kBN / 16 / kPChunks) + kq;
+              umma_ts_elect(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
+                            mnmajor_desc(v_addr, kk), kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
             }
-            const uint32_t k_addr = ring_addr + sk * kTileBytes;
+          }
+          if (!ok) break;
+          if (t == kQTiles - 1) umma_commit_elect(&sb->kv_empty[sv]);
+          if (more) {
+            if (t == 0) {
+              ok = __all_sync(0xffffffffu, mbar_wait(&sb->kv_full[sk], (ik / kSlots) & 1, guard));
+              if (!ok) break;
+              tc_fence_after();
+            }
 #pragma unroll
             for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-              umma_ss(tmem + t * 128, kmajor_desc(q_addr + t * kTileBytes, kk), kmajor_desc(k_addr, kk),
-                      kIdescQK, kk > 0);
+              umma_ss_elect(tmem + t * 128, kmajor_desc(q_addr + t * kTileBytes, kk),
+                            kmajor_desc(k_addr, kk), kIdescQK, kk > 0);
             }
-            umma_commit(&sb->s_full[t]);
-            if (t == kQTiles - 1) umma_commit(&sb->kv_empty[sk]);
+            umma_commit_elect(&sb->s_full[t]);
+            if (t == kQTiles - 1) umma_commit_elect(&sb->kv_empty[sk]);
           } else {
-            umma_commit(&sb->o_full[t]);
+            umma_commit_elect(&sb->o_full[t]);
           }
         }
       }
-      // Every MMA this thread issued has completed before TMEM may be released.
-      umma_commit(&sb->mma_done);
+      // Every MMA issued has completed before TMEM may be released.
+      umma_commit_elect(&sb->mma_done);
       mbar_wait(&sb->mma_done, 0, guard);
+      FLB_TRACE(3)
     }
-  } else {
+    FLB_TRACE_DUMP("mma(0=wait_kv,1=wait_p,2=issue,3=drain)")
+  } else if (warp < kProducerWarp) {
     // ------------------------------- softmax warpgroups -------------------------------
+#ifdef FLB_PREFILL_REGSPLIT
+    warpgroup_regs_inc<kSoftmaxRegs>();
+#endif
     const int t = warp >> 2;                  // Q tile of this warpgroup
     const int quarter = warp & 3;             // TMEM lane quarter this warp may access
     const int row_in_tile = quarter * 32 + lane;
@@ -283,11 +380,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_ref = -INFINITY;  // log2-domain reference point of this row
     float l_sum = 0.f;
     bool ok = true;
+    FLB_TRACE_DECL
     for (int j = 0; j < n_kv; ++j) {
+      FLB_TRACE(6)
       if (!mbar_wait(&sb->s_full[t], j & 1, guard)) {
         ok = false;
         break;
       }
+      FLB_TRACE(0)
       tc_fence_after();
       uint32_t s[128];
       tmem_ld32(taddr_s + 0, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
@@ -295,6 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(taddr_s + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
       tmem_ld32(taddr_s + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
       tmem_ld_wait();
+      FLB_TRACE(1)
       float* sf = reinterpret_cast<float*>(s);
 
       const int k0 = j * kBN;
@@ -308,10 +409,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (c >= visible) sf[c] = -INFINITY;
         }
       }
-      float mx4[4] = {sf[0], sf[1], sf[2], sf[3]};
+      // Row max: 8 independent chains of 3-input maxima over columns 16..127, seeded by 0..15.
+      float mx8[8];
 #pragma unroll
-      for (int c = 4; c < 128; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], sf[c]);
-      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      for (int i = 0; i < 8; ++i) mx8[i] = fmaxf(sf[i], sf[i + 8]);
+#pragma unroll
+      for (int c = 16; c < 128; c += 16) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx8[i] = fmax3(mx8[i], sf[c + 2 * i], sf[c + 2 * i + 1]);
+      }
+      const float mx = fmaxf(fmax3(mx8[0], mx8[1], mx8[2]),
+                             fmaxf(fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float mt = mx == -INFINITY ? -INFINITY : mx * sl2;
 
       float m_new = m_ref;
@@ -321,42 +429,38 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (rescale) l_sum *= factor;
       m_ref = m_new;
       const float ref = m_ref == -INFINITY ? 0.f : m_ref;
-
-      // P over the first 64 columns of this S region (already read into registers), in halves
-      // so only 32 packed registers are live next to the scores.
-      float ps[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const int i = half * 64 + 2 * c;
-          const float p0 = ex2(fmaf(sf[i], sl2, -ref));
-          const float p1 = ex2(fmaf(sf[i + 1], sl2, -ref));
-          ps[c & 3] += p0 + p1;
-          pk[c] = pack2<T>(p0, p1);
-        }
-        tmem_st32(taddr_s + half * 32, pk);
-      }
-      l_sum += (ps[0] + ps[1]) + (ps[2] + ps[3]);
       if (__any_sync(0xffffffffu, rescale)) {
-        // O holds PV through tile j-1 (its completion is covered by s_full) and PV of tile j is
-        // not issued before p_full: rescale it in place now that the scores are dead.
+        // Rare: the reference point moved by more than the threshold. O holds PV through tile
+        // j-1 (its completion is covered by s_full) and PV of tile j waits for the first P half,
+        // so O is rescaled in place here, 16 columns at a time to keep registers for the scores.
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t ov[32];
-          tmem_ld32(taddr_o + c * 32, ov);
+        for (int c = 0; c < 8; ++c) {
+          uint32_t ov[16];
+          tmem_ld16(taddr_o + c * 16, ov);
           tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
+          for (int e = 0; e < 16; ++e) {
             ov[e] = __float_as_uint(__uint_as_float(ov[e]) * factor);
           }
-          tmem_st32(taddr_o + c * 32, ov);
+          tmem_st16(taddr_o + c * 16, ov);
         }
       }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&sb->p_full[t]);
+
+      // x = s * scale_log2 - ref on pairs; 2^x on the SFU for most pairs and, in tiles without
+      // masked scores, with the FMA-pipe polynomial for kPolyPairs of every 8 pairs (the choice
+      // is made once per tile so the unrolled loop has no branches). P is published to the MMA
+      // warp in kPChunks chunks as soon as each chunk is in TMEM.
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};
+      const float nref = -ref;
+      FLB_TRACE(2)
+      if (tile_needs_mask) {
+        softmax_exp_store<T, 0, kPChunks>(sf, sl2, nref, ps, taddr_s, sb->p_half[t]);
+      } else {
+        softmax_exp_store<T, kPolyPairs, kPChunks>(sf, sl2, nref, ps, taddr_s, sb->p_half[t]);
+      }
+      l_sum += (ps[0] + ps[1]) + (ps[2] + ps[3]);
+      FLB_TRACE(3)
+      FLB_TRACE(4)
     }
 
     // Epilogue: O / l in the input dtype, and the natural-log LSE.
@@ -390,6 +494,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             l_sum > 0.f ? m_ref * 0.69314718055994530942f + logf(l_sum) : -INFINITY;
       }
     }
+    FLB_TRACE(5)
+    FLB_TRACE_DUMP("softmax(0=wait_s,1=ld,2=max+rescale,3=exp+st,4=-,5=epilogue,6=loop)")
   }
 
   tc_fence_before();
@@ -401,20 +507,57 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // One shared-memory opt-in per (kernel instantiation, device) and host thread.
-template <typename T>
-int launch_prefill(const PrefillArgs& a, const CUtensorMap& tmq, const CUtensorMap& tmk,
+template <typename T, int kPoly, int kChunks>
+int launch_variant(const PrefillArgs& a, const CUtensorMap& tmq, const CUtensorMap& tmk,
                    const CUtensorMap& tmv, int grid, int dev, cudaStream_t stream) {
   static thread_local int configured_device = -1;
   if (configured_device != dev) {
-    if (int st = check_cuda(cudaFuncSetAttribute(prefill_kernel<T>,
+    if (int st = check_cuda(cudaFuncSetAttribute(prefill_kernel<T, kPoly, kChunks>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  kSmemBytes),
                             "cudaFuncSetAttribute(prefill)"))
       return st;
     configured_device = dev;
   }
-  prefill_kernel<T><<<grid, kThreads, kSmemBytes, stream>>>(a, tmq, tmk, tmv);
+  prefill_kernel<T, kPoly, kChunks><<<grid, kThreads, kSmemBytes, stream>>>(a, tmq, tmk, tmv);
   return check_cuda(cudaGetLastError(), "prefill_kernel launch");
+}
+
+// Tuning knobs read once per process: FLASH_LAB_PREFILL_POLY_PAIRS=0|2|3|4 (pairs of every 8
+// whose 2^x runs on the FMA pipe) and FLASH_LAB_PREFILL_P_CHUNKS=1|2 (chunks P is published in).
+int env_choice(const char* name, int fallback, int a, int b, int c, int d) {
+  const char* env = std::getenv(name);
+  if (env == nullptr) return fallback;
+  const int v = std::atoi(env);
+  return (v == a || v == b || v == c || v == d) ? v : fallback;
+}
+
+int poly_pairs() {
+  static const int value = env_choice("FLASH_LAB_PREFILL_POLY_PAIRS", kDefaultPolyPairs, 0, 2, 3, 4);
+  return value;
+}
+
+int p_chunks() {
+  static const int value = env_choice("FLASH_LAB_PREFILL_P_CHUNKS", kDefaultPChunks, 1, 2, 1, 2);
+  return value;
+}
+
+template <typename T, int kChunks>
+int launch_poly(const PrefillArgs& a, const CUtensorMap& tmq, const CUtensorMap& tmk,
+                const CUtensorMap& tmv, int grid, int dev, cudaStream_t stream) {
+  switch (poly_pairs()) {
+    case 0: return launch_variant<T, 0, kChunks>(a, tmq, tmk, tmv, grid, dev, stream);
+    case 2: return launch_variant<T, 2, kChunks>(a, tmq, tmk, tmv, grid, dev, stream);
+    case 3: return launch_variant<T, 3, kChunks>(a, tmq, tmk, tmv, grid, dev, stream);
+    default: return launch_variant<T, 4, kChunks>(a, tmq, tmk, tmv, grid, dev, stream);
+  }
+}
+
+template <typename T>
+int launch_prefill(const PrefillArgs& a, const CUtensorMap& tmq, const CUtensorMap& tmk,
+                   const CUtensorMap& tmv, int grid, int dev, cudaStream_t stream) {
+  if (p_chunks() == 1) return launch_poly<T, 1>(a, tmq, tmk, tmv, grid, dev, stream);
+  return launch_poly<T, 2>(a, tmq, tmk, tmv, grid, dev, stream);
 }
 
 int validate(const flb_attn_params* p) {
