@@ -34,7 +34,6 @@ import math
 import os
 import pathlib
 import statistics
-import subprocess
 import sys
 import threading
 import time
@@ -79,61 +78,64 @@ def load_traffic() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons while the timed region runs."""
+    """SM clock and throttle reasons sampled through NVML every 5 ms while the timed region runs
+    (nvidia-smi's own loop is too coarse for a ~20 ms region). Reads only; changes nothing."""
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {  # NVML clocks-event-reason bits
+        "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80,
+    }
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, period_s: float = 0.005):
         self.index = index
-        self.proc = None
-        self.lines: list[str] = []
-        self.thread = None
+        self.period = period_s
+        self.samples: list[tuple[float, int, float]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._nvml = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except OSError:
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            handle = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+
+            def loop():
+                while not self._stop.is_set():
+                    try:
+                        clk = pynvml.nvmlDeviceGetClockInfo(handle, pynvml.NVML_CLOCK_SM)
+                        rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(handle)
+                        pw = pynvml.nvmlDeviceGetPowerUsage(handle) / 1000.0
+                        self.samples.append((float(clk), int(rs), pw))
+                    except Exception:  # noqa: BLE001 - sampling must never break the bench
+                        pass
+                    self._stop.wait(self.period)
+
+            self._thread = threading.Thread(target=loop, daemon=True)
+            self._thread.start()
+        except Exception:  # noqa: BLE001 - no NVML: report no samples
+            self._nvml = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            if self.thread is not None:
-                self.thread.join(timeout=2)
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=2)
 
     def summary(self) -> dict:
-        sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax = float(parts[2])
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower() in ("active", "1"):
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        sm = [c for c, _, _ in self.samples]
+        reasons = sorted({name for _, r, _ in self.samples for name, bit in self.REASONS.items()
+                          if r & bit})
+        power = [p for _, _, p in self.samples]
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(self.max_mhz) if self.max_mhz else None,
+                "reasons": reasons, "samples": len(sm),
+                "power_w_median": statistics.median(power) if power else None,
+                "source": "NVML, 5 ms period, during the timed region"}
 
 
 def time_steps(fn, steps: int, warmup: int, dist=None, device=None):
@@ -351,8 +353,11 @@ def run_extra(torch, flash_lab, device, dist, world, rank, args, peaks, traffic)
     ms = time_steps(lambda: flash_lab.attention(q, k, v, causal=True), args.steps, args.warmup,
                     dist, device)
     achieved = flops / (ms * 1e-3) / 1e12
+    tr = traffic.get("prefill_kernel_causal")
     out["prefill_causal"] = {"value": world * achieved, "unit": "TFLOP/s", "ms_per_step": ms,
-                             "roofline_frac": achieved / peaks["bf16_tflops"]}
+                             "roofline_frac": achieved / peaks["bf16_tflops"],
+                             "traffic": tr.get("bytes_per_launch") if tr else None,
+                             "flop_per_call": flops}
     del q, k, v
 
     l2_flush = torch.empty(512 * 2**20, dtype=torch.uint8, device=device)
