@@ -74,6 +74,8 @@ SIGNATURES = {
     "flb_decode_merge": ([_p, _p, _i32, _i32, _i32, _i32, _i32, _p, _i64, _i64, _p, _p],
                          ctypes.c_int),
     "flb_selftest_umma": ([_p, _p, _p, _p, _p, _p, _p, _p], ctypes.c_int),
+    "flb_decode_fwd_static": ([ctypes.POINTER(DecodeParams), _p], ctypes.c_int),
+    "flb_decode_static_scratch_bytes": ([], ctypes.c_size_t),
 }
 
 _LIB: ctypes.CDLL | None = None

@@ -134,6 +134,27 @@ size_t flb_decode_workspace_bytes(int32_t batch, int32_t heads, int32_t head_dim
 int flb_decode_fwd(const flb_decode_params* params, flb_stream_t stream);
 
 /*
+ * Allocation-free decode step. No counterpart in the reference: this entry point is an
+ * addition for callers that cannot allocate device memory when they decode. cudaMalloc may
+ * synchronise the device and is not allowed during CUDA-graph stream capture, and a serving loop
+ * that plans its memory up front may forbid allocation altogether. It computes exactly what
+ * flb_decode_fwd computes (the same kernels, the same split count), but keeps the split partials
+ * in a static device array of flb_decode_static_scratch_bytes() bytes (8 MiB) instead of a
+ * caller workspace; params->workspace is ignored. Problems whose partials do not fit
+ * (B * H * splits * (head_dim + 2) * 4 bytes, rounded) return FLB_ERR_WORKSPACE without
+ * launching.
+ * Every GPU that loads the library holds the array until exit. All calls on a device share it
+ * and it keeps the last call's contents (nothing needs to start at zero), so calls that overlap
+ * on the GPU race. The first call on a device looks up the array's address with that device
+ * current; make it before any stream capture. It calls no cudaMalloc, cudaFree or other
+ * allocating routine.
+ */
+int flb_decode_fwd_static(const flb_decode_params* params, flb_stream_t stream);
+
+/* Capacity in bytes of the static scratch array of flb_decode_fwd_static. */
+size_t flb_decode_static_scratch_bytes(void);
+
+/*
  * Raw split partials for a cross-GPU merge: runs the decode kernel on this device's keys
  * [key_begin, key_end) of every sequence (clamped to its length), cut into `num_splits` ranges
  * of the same rounding as flb_decode_fwd, and writes
