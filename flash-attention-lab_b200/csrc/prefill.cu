@@ -208,13 +208,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int hkv = h / a.group;
   const int q0 = qb * kRowsPerCta;
 
+  // KV tiles each Q tile needs: all of them, or up to the last key its last row sees (causal).
+  // The CTA streams the larger count; Q tile 0 of a causal CTA stops earlier.
   const int kv_tiles_all = (a.seqlen_k + kBN - 1) / kBN;
-  int n_kv = kv_tiles_all;
-  if (a.causal) {
-    const int last_row = min(q0 + kRowsPerCta, a.seqlen_q) - 1;
-    const int max_key = last_row + a.causal_offset;  // last key any row of the CTA sees
-    n_kv = max_key < 0 ? 0 : min(kv_tiles_all, max_key / kBN + 1);
+  int n_kv_tile[kQTiles];
+#pragma unroll
+  for (int t = 0; t < kQTiles; ++t) {
+    n_kv_tile[t] = kv_tiles_all;
+    if (a.causal) {
+      const int last_row = min(q0 + (t + 1) * kBM, a.seqlen_q) - 1;
+      const int max_key = last_row + a.causal_offset;  // last key any row of the tile sees
+      n_kv_tile[t] = max_key < 0 ? 0 : min(kv_tiles_all, max_key / kBN + 1);
+    }
   }
+  const int n_kv = max(n_kv_tile[0], n_kv_tile[1]);
 
   if (threadIdx.x == 0) {
     sb->abort_flag = 0;
@@ -281,7 +288,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     FLB_TRACE_DUMP("producer(0=wait_empty,1=issue)")
   } else if (warp == kMmaWarp) {
-    FLB_TRACE_DECL
     // ------------------------------- MMA issuer -------------------------------
     // The whole warp runs this loop (waits and descriptors stay warp-uniform); elect.sync picks
     // the one lane that issues each tcgen05.mma / commit.
@@ -298,6 +304,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
 #pragma unroll
         for (int t = 0; t < kQTiles; ++t) {
+          if (n_kv_tile[t] == 0) continue;
 #pragma unroll
           for (int kk = 0; kk < kHeadDim / 16; ++kk) {
             umma_ss_elect(tmem + t * 128, kmajor_desc(q_addr + t * kTileBytes, kk),
@@ -312,37 +319,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int sv = iv % kSlots;
         const int ik = 2 * j + 2;  // K_{j+1} ring index
         const int sk = ik % kSlots;
-        const bool more = j + 1 < n_kv;
         FLB_TRACE(2)
         ok = __all_sync(0xffffffffu, mbar_wait(&sb->kv_full[sv], (iv / kSlots) & 1, guard));
         if (!ok) break;
         FLB_TRACE(0)
         const uint32_t v_addr = ring_addr + sv * kTileBytes;
         const uint32_t k_addr = ring_addr + sk * kTileBytes;
+        bool k_ready = false;
 #pragma unroll
         for (int t = 0; t < kQTiles; ++t) {
-          // P arrives in kPChunks chunks of keys; each chunk's k-steps are issued as soon as
-          // the softmax warpgroup has stored it.
+          if (j < n_kv_tile[t]) {
+            // P arrives in kPChunks chunks of keys; each chunk's k-steps are issued as soon as
+            // the softmax warpgroup has stored it.
 #pragma unroll
-          for (int ch = 0; ch < kPChunks; ++ch) {
-            ok = __all_sync(0xffffffffu, mbar_wait(&sb->p_half[t][ch], j & 1, guard));
-            if (!ok) break;
-            FLB_TRACE(1)
-            tc_fence_after();
+            for (int ch = 0; ch < kPChunks; ++ch) {
+              ok = __all_sync(0xffffffffu, mbar_wait(&sb->p_half[t][ch], j & 1, guard));
+              if (!ok) break;
+              FLB_TRACE(1)
+              tc_fence_after();
 #pragma unroll
-            for (int kq = 0; kq < kBN / 16 / kPChunks; ++kq) {
-              const int kk = ch * (kBN / 16 / kPChunks) + kq;
-              umma_ts_elect(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
-                            mnmajor_desc(v_addr, kk), kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+              for (int kq = 0; kq < kBN / 16 / kPChunks; ++kq) {
+                const int kk = ch * (kBN / 16 / kPChunks) + kq;
+                umma_ts_elect(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
+                              mnmajor_desc(v_addr, kk), kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+              }
             }
+            if (!ok) break;
           }
-          if (!ok) break;
+          // V_j is released once the last tile that uses it (always tile 1, whose range is the
+          // CTA's) has its PV issued; K_{j+1} once tile 1's S for it is issued.
           if (t == kQTiles - 1) umma_commit_elect(&sb->kv_empty[sv]);
-          if (more) {
-            if (t == 0) {
+          if (j + 1 < n_kv_tile[t]) {
+            if (!k_ready) {
               ok = __all_sync(0xffffffffu, mbar_wait(&sb->kv_full[sk], (ik / kSlots) & 1, guard));
               if (!ok) break;
               tc_fence_after();
+              k_ready = true;
             }
 #pragma unroll
             for (int kk = 0; kk < kHeadDim / 16; ++kk) {
@@ -350,10 +362,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                             kmajor_desc(k_addr, kk), kIdescQK, kk > 0);
             }
             umma_commit_elect(&sb->s_full[t]);
-            if (t == kQTiles - 1) umma_commit_elect(&sb->kv_empty[sk]);
-          } else {
+          } else if (j + 1 == n_kv_tile[t]) {
             umma_commit_elect(&sb->o_full[t]);
           }
+          if (t == kQTiles - 1 && j + 1 < n_kv) umma_commit_elect(&sb->kv_empty[sk]);
         }
       }
       // Every MMA issued has completed before TMEM may be released.
@@ -381,7 +393,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     float l_sum = 0.f;
     bool ok = true;
     FLB_TRACE_DECL
-    for (int j = 0; j < n_kv; ++j) {
+    const int n_kv_t = n_kv_tile[t];
+    for (int j = 0; j < n_kv_t; ++j) {
       FLB_TRACE(6)
       if (!mbar_wait(&sb->s_full[t], j & 1, guard)) {
         ok = false;
@@ -464,7 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     // Epilogue: O / l in the input dtype, and the natural-log LSE.
-    if (ok && n_kv > 0) ok = mbar_wait(&sb->o_full[t], 0, guard);
+    if (ok && n_kv_t > 0) ok = mbar_wait(&sb->o_full[t], 0, guard);
     if (ok) {
       tc_fence_after();
       const bool row_ok = row < a.seqlen_q;
@@ -475,7 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t ov[32];
-        if (n_kv > 0) {
+        if (n_kv_t > 0) {
           tmem_ld32(taddr_o + c * 32, ov);
           tmem_ld_wait();
         } else {
