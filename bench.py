@@ -401,6 +401,49 @@ def run_extra(torch, flash_lab, device, dist, world, rank, args, peaks, traffic)
                      f"S_max=32768 D=128 lengths={'32768' if lens_kind == 'full' else lens}",
                      "l2": "512 MB buffer zeroed before every call (outside the events)"}
         del qd, kc, vc
+
+    # B=1 MHA at 32K with the KV sequence split across the ranks (decode_sharded: per-rank
+    # partials, NCCL all_gather, fixed-order merge); on one rank it is the plain split decode.
+    from flash_lab import _capi
+    from flash_lab.distributed import ShardSpec, decode_sharded
+
+    smax, hh, hk = 32768, 32, 32
+    shard = ShardSpec.even(smax, world, rank)
+    gen = torch.Generator(device=device).manual_seed(17)  # same cache on every rank
+    qd = torch.randn(1, hh, d, device=device, dtype=torch.bfloat16, generator=gen)
+    full_k = torch.randn(1, smax, hk, d, device=device, dtype=torch.bfloat16, generator=gen)
+    full_v = torch.randn(1, smax, hk, d, device=device, dtype=torch.bfloat16, generator=gen)
+    k_shard = full_k[:, shard.offset:shard.offset + shard.length].contiguous()
+    v_shard = full_v[:, shard.offset:shard.offset + shard.length].contiguous()
+    del full_k, full_v
+    seq_lens = torch.full((1,), smax, device=device, dtype=torch.int32)
+    sm = torch.cuda.get_device_properties(device).multi_processor_count
+    splits = _capi.load().flb_decode_num_splits(1, hh, hk, d, shard.length, sm)
+    times = []
+    for i in range(args.warmup + args.steps):
+        l2_flush.zero_()
+        if dist is not None:
+            dist.barrier()
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st.record()
+        decode_sharded(qd, k_shard, v_shard, seq_lens, shard, splits_per_rank=splits)
+        en.record()
+        if i >= args.warmup:
+            times.append((st, en))
+    torch.cuda.synchronize(device)
+    ms = statistics.median(a.elapsed_time(b) for a, b in times)
+    if dist is not None:
+        t = torch.tensor([ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    nbytes = decode_bytes(hh, hk, d, [smax], 1)
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    out["decode_b1_split"] = {
+        "value": gbs, "unit": "GB/s", "ms_per_step": ms, "bytes_per_call": nbytes,
+        "per_gpu_roofline_frac": gbs / world / peaks["hbm_gbs"], "scaling": "strong",
+        "config": f"B=1 H=H_kv=32 D=128 32K keys split over {world} GPU(s), {splits} splits "
+                  f"per GPU, partials all-gathered over NCCL and merged in a fixed order",
+        "l2": "512 MB buffer zeroed before every call (outside the events)"}
     return out
 
 

@@ -1,0 +1,217 @@
+"""Long-context decode split along the KV sequence across ranks (flash_lab.distributed).
+
+CPU part: two gloo ranks run decode_sharded end to end with the kernel steps replaced by numpy
+restatements (the oracle's partials and merge, test infrastructure only), which checks the
+plumbing: shard offsets, device-side local lengths, the all_gather in rank order and the merge
+layout, against the oracle's unsplit decode.
+
+GPU part (one GPU): the real kernels on emulated shards. Partials computed shard by shard and
+merged are bitwise equal to partials of the same global key windows computed on the full cache,
+and within tolerance of the oracle. A two-GPU NCCL test runs when two GPUs are visible.
+"""
+
+import ctypes
+import math
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import oracle
+from flash_lab import _capi
+from flash_lab.distributed import ShardSpec, decode_sharded, local_lengths, merge_partials
+
+TILE = 64  # keys per decode tile: split ranges are whole numbers of tiles
+
+
+def numpy_partials(q3, k_shard, v_shard, lens, splits, scale):
+    """Reference partials with the kernel's split boundaries (fp64 on the CPU)."""
+    q = q3.double().numpy()
+    k = k_shard.double().numpy()
+    v = v_shard.double().numpy()
+    batch, heads, head_dim = q.shape
+    group = heads // k.shape[2]
+    po = np.zeros((batch, heads, splits, head_dim))
+    pml = np.zeros((batch, heads, splits, 2))
+    pml[..., 0] = -np.inf
+    for b in range(batch):
+        n = int(lens[b])
+        if n <= 0:
+            continue
+        per = -(-(-(-n // splits)) // TILE) * TILE
+        for s in range(splits):
+            k0, k1 = s * per, min(n, s * per + per)
+            if k1 <= k0:
+                continue
+            for h in range(heads):
+                x = (k[b, k0:k1, h // group] @ q[b, h]) * scale / math.log(2.0)
+                m = x.max()
+                p = np.exp2(x - m)
+                po[b, h, s] = p @ v[b, k0:k1, h // group]
+                pml[b, h, s] = (m, p.sum())
+    return torch.from_numpy(po), torch.from_numpy(pml)
+
+
+def numpy_merge(po, pml, dtype):
+    o, lse = oracle.merge_partials(po.numpy(), pml[..., 0].numpy(), pml[..., 1].numpy())
+    return torch.from_numpy(o), torch.from_numpy(lse)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _cpu_rank(rank, world, port, inputs, results):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        q, kc, vc, lens = inputs
+        shard = ShardSpec.even(kc.shape[1], world, rank)
+        k_shard = kc[:, shard.offset:shard.offset + shard.length]
+        v_shard = vc[:, shard.offset:shard.offset + shard.length]
+        o, lse = decode_sharded(q, k_shard, v_shard, lens, shard, splits_per_rank=3,
+                                return_lse=True, _partials=numpy_partials, _merge=numpy_merge)
+        results[rank] = (o.numpy(), lse.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_match_the_oracle():
+    gen = torch.Generator().manual_seed(0)
+    batch, heads, heads_kv, smax, d = 2, 4, 2, 500, 16
+    q = torch.randn(batch, heads, d, generator=gen, dtype=torch.float64)
+    kc = torch.randn(batch, smax, heads_kv, d, generator=gen, dtype=torch.float64)
+    vc = torch.randn(batch, smax, heads_kv, d, generator=gen, dtype=torch.float64)
+    lens = torch.tensor([500, 203], dtype=torch.int32)   # the second ends inside shard 0
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as manager:
+        results = manager.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_cpu_rank, args=(r, 2, port, (q, kc, vc, lens), results))
+                 for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=120)
+            assert p.exitcode == 0
+        out = dict(results)
+    ref, ref_lse = oracle.decode(q.numpy(), kc.numpy(), vc.numpy(), lens.numpy(),
+                                 return_lse=True)
+    for rank in range(2):
+        o, lse = out[rank]
+        np.testing.assert_allclose(o, ref, rtol=0, atol=1e-12)
+        np.testing.assert_allclose(lse, ref_lse, rtol=0, atol=1e-12)
+
+
+def test_shards_cover_the_sequence():
+    for smax, world in [(32768, 8), (1000, 3), (5, 4)]:
+        shards = [ShardSpec.even(smax, world, r) for r in range(world)]
+        assert shards[0].offset == 0
+        assert sum(s.length for s in shards) == smax
+        for a, b in zip(shards, shards[1:]):
+            assert a.offset + a.length == b.offset
+    lens = torch.tensor([0, 10, 600, 1000], dtype=torch.int32)
+    got = local_lengths(lens, ShardSpec(334, 333))
+    assert got.tolist() == [0, 0, 266, 333]
+
+
+def _window_partials(q3, kc, vc, lens, key_begin, key_end, splits, scale):
+    """The library's partials of one global key window on the full cache (one GPU)."""
+    lib = _capi.load()
+    batch, heads, head_dim = q3.shape
+    po = torch.empty((batch, heads, splits, head_dim), device="cuda", dtype=torch.float32)
+    pml = torch.empty((batch, heads, splits, 2), device="cuda", dtype=torch.float32)
+    p = _capi.DecodeParams(
+        q3.data_ptr(), kc.data_ptr(), vc.data_ptr(), 0, 0, lens.data_ptr(),
+        q3.stride(0), q3.stride(1), kc.stride(0), kc.stride(1), kc.stride(2),
+        vc.stride(0), vc.stride(1), vc.stride(2), 0, 0,
+        batch, heads, kc.shape[2], head_dim, kc.shape[1], splits, _capi.FLB_BF16, scale, 0, 0,
+        0)
+    rc = lib.flb_decode_partials(ctypes.byref(p), key_begin, key_end, po.data_ptr(),
+                                 pml.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, _capi.error_message(lib, rc)
+    return po, pml
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world,splits", [(2, 1), (4, 2), (8, 1)])
+def test_emulated_shards_are_bitwise_equal_to_global_windows(world, splits):
+    gen = torch.Generator(device="cuda").manual_seed(world)
+    batch, heads, heads_kv, smax, d = 1, 32, 32, 32768, 128
+    q = torch.randn(batch, heads, d, device="cuda", dtype=torch.bfloat16, generator=gen)
+    kc = torch.randn(batch, smax, heads_kv, d, device="cuda", dtype=torch.bfloat16, generator=gen)
+    vc = torch.randn(batch, smax, heads_kv, d, device="cuda", dtype=torch.bfloat16, generator=gen)
+    lens = torch.tensor([smax - 1000], device="cuda", dtype=torch.int32)
+    scale = 1.0 / math.sqrt(d)
+    from flash_lab.distributed import shard_partials
+
+    shard_po, shard_pml, win_po, win_pml = [], [], [], []
+    for r in range(world):
+        shard = ShardSpec.even(smax, world, r)
+        ks = kc[:, shard.offset:shard.offset + shard.length].contiguous()
+        vs = vc[:, shard.offset:shard.offset + shard.length].contiguous()
+        po, pml = shard_partials(q, ks, vs, local_lengths(lens, shard), splits, scale)
+        shard_po.append(po)
+        shard_pml.append(pml)
+        po, pml = _window_partials(q, kc, vc, lens, shard.offset, shard.offset + shard.length,
+                                   splits, scale)
+        win_po.append(po)
+        win_pml.append(pml)
+    o_shards, lse_shards = merge_partials(torch.cat(shard_po, 2), torch.cat(shard_pml, 2),
+                                          torch.bfloat16)
+    o_win, lse_win = merge_partials(torch.cat(win_po, 2), torch.cat(win_pml, 2), torch.bfloat16)
+    assert torch.equal(o_shards, o_win) and torch.equal(lse_shards, lse_win)
+    ref, ref_lse = oracle.decode(q.double().cpu().numpy(), kc.double().cpu().numpy(),
+                                 vc.double().cpu().numpy(), lens.cpu().numpy(), return_lse=True)
+    err = np.abs(o_shards.double().cpu().numpy() - ref).max()
+    rounding = np.abs(torch.from_numpy(ref).bfloat16().double().numpy() - ref).max()
+    assert err <= 2 * rounding, (err, rounding)
+    assert np.abs(lse_shards.double().cpu().numpy() - ref_lse).max() < 1e-3
+
+
+def _nccl_rank(rank, world, port, seed):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    import datetime
+
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        gen = torch.Generator(device="cuda").manual_seed(seed)
+        q = torch.randn(1, 32, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+        kc = torch.randn(1, 8192, 8, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+        vc = torch.randn(1, 8192, 8, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+        lens = torch.tensor([8000], device="cuda", dtype=torch.int32)
+        shard = ShardSpec.even(8192, world, rank)
+        o = decode_sharded(q, kc[:, shard.offset:shard.offset + shard.length],
+                           vc[:, shard.offset:shard.offset + shard.length], lens, shard,
+                           splits_per_rank=2)
+        torch.cuda.synchronize()
+        ref = oracle.decode(q.double().cpu().numpy(), kc.double().cpu().numpy(),
+                            vc.double().cpu().numpy(), lens.cpu().numpy())
+        err = np.abs(o.double().cpu().numpy() - ref).max()
+        rounding = np.abs(torch.from_numpy(ref).bfloat16().double().numpy() - ref).max()
+        assert err <= 2 * rounding, (rank, err, rounding)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_two_gpus_over_nccl():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_nccl_rank, args=(r, 2, port, 5)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0
