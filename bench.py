@@ -216,10 +216,32 @@ def run_reference_arm(args) -> None:
         "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
+
+
+_JSON_OUT = None
+
+
+def emit(line: dict) -> None:
+    """Writes the one JSON result line to the real stdout (everything else goes to stderr)."""
+    out = _JSON_OUT if _JSON_OUT is not None else sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
+def _claim_stdout() -> None:
+    """Points file descriptor 1 at stderr so library chatter (NCCL's banner, warnings) cannot
+    precede the result line, and keeps the original stdout for emit()."""
+    global _JSON_OUT
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    _JSON_OUT = os.fdopen(saved, "w", buffering=1)
+    sys.stdout = sys.stderr
 
 
 def main() -> int:
+    _claim_stdout()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -334,7 +356,7 @@ def main() -> int:
             "cpu_baseline": cpu,
             "extra": extra,
         }
-        print(json.dumps(line), flush=True)
+        emit(line)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
