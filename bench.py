@@ -253,9 +253,15 @@ def main() -> int:
                     choices=["prefill", "prefill_causal", "decode_mha", "decode_gqa"],
                     help="run only warmup + steps launches of one kernel (for ncu captures)")
     ap.add_argument("--batch", type=int, default=None, help="batch size of --profile")
+    ap.add_argument("--e2e-llama", action="store_true",
+                    help="end-to-end Llama-3.1-8B-architecture generation (BASELINE config 5)")
+    ap.add_argument("--new-tokens", type=int, default=256)
+    ap.add_argument("--prompt-len", type=int, default=8192)
     args = ap.parse_args()
     if args.profile is not None:
         return run_profile_case(args)
+    if args.e2e_llama:
+        return run_e2e_llama(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
@@ -467,6 +473,76 @@ def run_extra(torch, flash_lab, device, dist, world, rank, args, peaks, traffic)
                   f"per GPU, partials all-gathered over NCCL and merged in a fixed order",
         "l2": "512 MB buffer zeroed before every call (outside the events)"}
     return out
+
+
+def run_e2e_llama(args) -> int:
+    """Llama-3.1-8B architecture (32 layers, d_model 4096, 32 heads, 8 KV
+    heads, head_dim 128, RoPE theta 500000, vocab 128256) with random-init bf16 weights, batch 1,
+    a random 8192-token prompt, 256 greedy tokens, a static KV cache and the decode step compiled
+    (torch.compile fullgraph, CUDA graphs), attention through the flash_lab HF backend; the same
+    run with transformers' SDPA backend beside it. Prints one JSON line."""
+    import torch
+    from transformers import CompileConfig, LlamaConfig, LlamaForCausalLM, StaticCache
+
+    import flash_lab.hf
+
+    flash_lab.hf.register()
+    device = torch.device("cuda", 0)
+    cfg = LlamaConfig(vocab_size=128256, hidden_size=4096, intermediate_size=14336,
+                      num_hidden_layers=32, num_attention_heads=32, num_key_value_heads=8,
+                      head_dim=128, rope_theta=500000.0, max_position_embeddings=131072)
+    torch.manual_seed(0)
+    with torch.device(device):
+        model = LlamaForCausalLM(cfg)
+    model = model.to(torch.bfloat16).eval()
+    ids = torch.randint(0, 128000, (1, args.prompt_len),
+                        generator=torch.Generator().manual_seed(0)).to(device)
+    mask = torch.ones_like(ids)
+    max_len = args.prompt_len + args.new_tokens
+    results = {}
+    tokens = {}
+    for attn in ("flash_lab", "sdpa"):
+        model.config._attn_implementation = attn
+        torch._dynamo.reset()
+        cache = StaticCache(config=cfg, max_cache_len=max_len)
+
+        def generate(n):
+            cache.reset()
+            return model.generate(ids, attention_mask=mask, max_new_tokens=n, do_sample=False,
+                                  past_key_values=cache, pad_token_id=0, min_new_tokens=n,
+                                  compile_config=CompileConfig(fullgraph=True))
+
+        with torch.no_grad():
+            generate(16)        # compiles the decode step
+            generate(16)
+
+            def timed(n):
+                torch.cuda.synchronize()
+                st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                st.record()
+                out = generate(n)
+                en.record()
+                torch.cuda.synchronize()
+                return st.elapsed_time(en), out
+
+            ttft = min(timed(1)[0] for _ in range(3))
+            total, out = timed(args.new_tokens)
+        results[attn] = {"ttft_ms": ttft, "total_ms": total,
+                         "decode_step_ms": (total - ttft) / (args.new_tokens - 1)}
+        tokens[attn] = out[0, ids.shape[1]:].tolist()
+    agree = sum(1 for a, b in zip(tokens["flash_lab"], tokens["sdpa"]) if a == b)
+    first_diff = next((i for i, (a, b) in enumerate(zip(tokens["flash_lab"], tokens["sdpa"]))
+                       if a != b), None)
+    line = {"metric": "e2e Llama-3.1-8B arch: decode step ms / TTFT ms (lower is better)",
+            "higher_is_better": False, "dtype": "bf16", "data": "synthetic (random init, "
+            "random prompt)", "config": {"model": "Llama-3.1-8B architecture",
+            "prompt_len": args.prompt_len, "new_tokens": args.new_tokens, "batch": 1,
+            "cache": "static", "decode": "torch.compile, CUDA graphs (transformers turns "
+            "fullgraph off for attention backends named flash*)"},
+            "flash_lab": results["flash_lab"], "sdpa": results["sdpa"],
+            "greedy_tokens_equal": agree, "first_divergence": first_diff}
+    emit(line)
+    return 0
 
 
 def run_profile_case(args) -> int:
