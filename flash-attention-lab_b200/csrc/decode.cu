@@ -93,6 +93,9 @@ __global__ void __launch_bounds__(kDecodeThreads)
     decode_split_kernel(const __grid_constant__ DecodeArgs a,
                         const __grid_constant__ CUtensorMap tmk,
                         const __grid_constant__ CUtensorMap tmv) {
+  // The merge kernel, launched as a programmatic dependent, may be scheduled once every CTA of
+  // this grid has started; it waits (griddepcontrol.wait) for this grid to finish and flush.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   using Cfg = DecodeCfg<D>;
   constexpr int kStages = Cfg::kStages;
   constexpr int kKSteps = D / 16;   // MMA k-steps over head_dim
@@ -380,6 +383,9 @@ __global__ void decode_merge_kernel(const float* __restrict__ partial_o,
                                     const float* __restrict__ partial_ml, int heads, int head_dim,
                                     int num_splits, T* o, int64_t o_batch_stride,
                                     int64_t o_head_stride, float* lse) {
+  // Launched as a programmatic dependent of the split kernel: wait for its writes first (a no-op
+  // when launched normally).
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int bh = blockIdx.x;
   const int b = bh / heads;
   const int h = bh - b * heads;
@@ -430,9 +436,22 @@ int launch_split(const DecodeArgs& args, const CUtensorMap& tmk, const CUtensorM
 template <typename T>
 int launch_merge(const float* po, const float* pml, int batch, int heads, int head_dim,
                  int splits, void* o, int64_t obs, int64_t ohs, float* lse, cudaStream_t stream) {
-  decode_merge_kernel<T><<<batch * heads, head_dim, 0, stream>>>(
-      po, pml, heads, head_dim, splits, static_cast<T*>(o), obs, ohs, lse);
-  return check_cuda(cudaGetLastError(), "decode_merge_kernel launch");
+  // Programmatic dependent launch: the merge grid is scheduled while the split kernel drains
+  // and waits (griddepcontrol.wait) for its results, which hides the launch gap between them.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(batch * heads);
+  cfg.blockDim = dim3(head_dim);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  T* out = static_cast<T*>(o);
+  return check_cuda(cudaLaunchKernelEx(&cfg, decode_merge_kernel<T>, po, pml, heads, head_dim,
+                                       splits, out, obs, ohs, lse),
+                    "decode_merge_kernel launch");
 }
 
 int validate(const flb_decode_params* p) {
@@ -526,6 +545,7 @@ int splits_for(int batch, int heads, int heads_kv, int head_dim, int max_seqlen,
       static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(kMaxSplits, max_seqlen / 256)));
   if (ctas >= 4 * slots) return 1;
   // Smallest split count giving >= 3 waves with a full-enough last wave; else about 4 waves.
+  // (Targeting 6 waves measured slower: more partials to merge and more CTA prologues.)
   for (int s = 1; s <= max_splits; ++s) {
     const double waves = static_cast<double>(ctas * s) / static_cast<double>(slots);
     if (waves < 3.0) continue;

@@ -9,10 +9,10 @@
 // B200 design (not a port):
 //  * CTA = 256 query rows of one (batch, head) as two 128-row Q tiles; one softmax warpgroup per
 //    Q tile. Warp 8 is the TMA producer, warp 9 issues every tcgen05.mma from one thread.
-//  * Q (once) and 128-key K / V tiles arrive by TMA in 128-byte-swizzled [128 x 64] boxes; K and
-//    V alternate through a 4-slot mbarrier ring.
-//  * TMEM (512 columns): S0 | S1 | O0 | O1, 128 fp32 columns each. S = Q K^T is an SS UMMA
-//    (M=128, N=128, K=16 steps). The softmax warpgroup reads its S row (thread = row = TMEM lane),
+//  * Q (once) and 128-key K / V tiles arrive by TMA in 128-byte-swizzled [128 x 64] boxes (two
+//    per tile at head_dim 128, one at 64); K and V alternate through a 128 KB mbarrier ring.
+//  * TMEM (512 columns): S0 | S1 | O0 | O1, 128 fp32 columns each (O uses head_dim of them).
+//    S = Q K^T is an SS UMMA (M=128, N=128, K=16 steps). The softmax warpgroup reads its S row (thread = row = TMEM lane),
 //    writes P as packed 16-bit pairs over the first 64 columns of the same S region, and O += P V
 //    is a TS UMMA with P taken from TMEM and V as an MN-major shared-memory operand.
 //  * The MMA thread interleaves the two Q tiles: PV0(j), S0(j+1), PV1(j), S1(j+1), so one tile's
@@ -60,14 +60,21 @@ namespace {
 
 constexpr int kBM = 128;                       // rows per Q tile
 constexpr int kBN = 128;                       // keys per K/V tile
-constexpr int kHeadDim = 128;
 constexpr int kQTiles = 2;                     // Q tiles per CTA
 constexpr int kRowsPerCta = kBM * kQTiles;
-constexpr int kSlots = 4;                      // K/V ring slots
-constexpr int kTileBytes = kBM * kHeadDim * 2; // 32 KB: two [128 x 64] swizzled boxes
-constexpr int kBoxBytes = kTileBytes / 2;
-constexpr int kSmemData = (kQTiles + kSlots) * kTileBytes;
-constexpr int kSmemBytes = kSmemData + 1024 + 256;
+constexpr int kBoxBytes = kBM * 64 * 2;        // one swizzled [128 x 64] 16-bit box: 16 KB
+
+// Per head dim: a [128 x D] tile is D / 64 boxes. The K/V ring holds 128 KB of tiles at either
+// head dim (4 slots of 32 KB at D = 128, 8 of 16 KB at D = 64), so one CTA fills an SM.
+template <int D>
+struct Geometry {
+  static_assert(D == 64 || D == 128, "head_dim 64 or 128");
+  static constexpr int kBoxes = D / 64;
+  static constexpr int kTileBytes = kBM * D * 2;
+  static constexpr int kSlots = D == 64 ? 8 : 4;
+  static constexpr int kSmemData = (kQTiles + kSlots) * kTileBytes;
+  static constexpr int kSmemBytes = kSmemData + 1024 + 256;
+};
 // Warps: softmax WG0 (0-3), WG1 (4-7), producer (8), MMA issuer (9). With FLB_PREFILL_REGSPLIT the
 // CTA has 12 warps and setmaxnreg moves registers from warpgroup 2 (producer, MMA, 2 spare) to
 // the softmax warpgroups: launch 168 x 3 warpgroups = 208 + 208 + 80 (+8 spare) per lane.
@@ -97,6 +104,7 @@ struct PrefillArgs {
   TmaCoords qc, kc, vc;
 };
 
+template <int kSlots>
 struct SharedBarriers {
   uint64_t q_full;
   uint64_t kv_full[kSlots];
@@ -113,23 +121,25 @@ __device__ __forceinline__ int tma_c(const TmaCoords& c, int slot, int s, int h,
   return c.pos_s == slot ? s : (c.pos_h == slot ? h : b);
 }
 
-// Loads a [128 rows x 128 dims] tile as two swizzled boxes.
+// Loads a [128 rows x D dims] tile as D / 64 swizzled boxes.
+template <int D>
 __device__ __forceinline__ void load_tile(uint8_t* dst, const CUtensorMap* map,
                                           const TmaCoords& c, uint64_t* bar, int row, int head,
                                           int b) {
 #pragma unroll
-  for (int box = 0; box < 2; ++box) {
+  for (int box = 0; box < Geometry<D>::kBoxes; ++box) {
     tma_load_4d(dst + box * kBoxBytes, map, bar, box * 64, tma_c(c, 1, row, head, b),
                 tma_c(c, 2, row, head, b), tma_c(c, 3, row, head, b));
   }
 }
 
-// K-major SW128 operand (Q or K tile): k-step kk (16 elements) of a [128 x 128] tile.
+// K-major SW128 operand (Q or K tile): k-step kk (16 elements) of a [128 x D] tile.
 __device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile_addr, int kk) {
   return umma_smem_desc_sw128(tile_addr + (kk >> 2) * kBoxBytes + (kk & 3) * 32, 16, 1024);
 }
 
-// MN-major SW128 operand (V tile, N = head_dim): k-step kk covers keys 16kk..16kk+15.
+// MN-major SW128 operand (V tile, N = head_dim): k-step kk covers keys 16kk..16kk+15; the
+// leading byte offset steps to the next 64 columns of N (unused at D = 64).
 __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile_addr, int kk) {
   return umma_smem_desc_sw128(tile_addr + kk * 2048, kBoxBytes, 1024);
 }
@@ -182,7 +192,7 @@ __device__ __forceinline__ void softmax_exp_store(const float* sf, float sl2, fl
   }
 }
 
-template <typename T, int kPolyPairs, int kPChunks>
+template <typename T, int D, int kPolyPairs, int kPChunks>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ PrefillArgs a, const __grid_constant__ CUtensorMap tmq,
                    const __grid_constant__ CUtensorMap tmk,
@@ -190,9 +200,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  constexpr int kTileBytes = Geometry<D>::kTileBytes;
+  constexpr int kSlots = Geometry<D>::kSlots;
   uint8_t* q_smem = smem;                               // kQTiles tiles
   uint8_t* ring = smem + kQTiles * kTileBytes;          // kSlots tiles
-  SharedBarriers* sb = reinterpret_cast<SharedBarriers*>(smem + kSmemData);
+  auto* sb = reinterpret_cast<SharedBarriers<kSlots>*>(smem + Geometry<D>::kSmemData);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -260,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmv);
       mbar_arrive_expect_tx(&sb->q_full, kQTiles * kTileBytes);
       for (int t = 0; t < kQTiles; ++t) {
-        load_tile(q_smem + t * kTileBytes, &tmq, a.qc, &sb->q_full, q0 + t * kBM, h, b);
+        load_tile<D>(q_smem + t * kTileBytes, &tmq, a.qc, &sb->q_full, q0 + t * kBM, h, b);
       }
       int issued = 0;
       bool ok = true;
@@ -275,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           FLB_TRACE(0)
           mbar_arrive_expect_tx(&sb->kv_full[slot], kTileBytes);
-          load_tile(ring + slot * kTileBytes, kind == 0 ? &tmk : &tmv, kind == 0 ? a.kc : a.vc,
+          load_tile<D>(ring + slot * kTileBytes, kind == 0 ? &tmk : &tmv, kind == 0 ? a.kc : a.vc,
                     &sb->kv_full[slot], j * kBN, hkv, b);
           issued = i + 1;
         }
@@ -295,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (n_kv > 0) {
       constexpr int kFmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
       constexpr uint32_t kIdescQK = umma_idesc_f16(kFmt, kBM, kBN, 0);
-      constexpr uint32_t kIdescPV = umma_idesc_f16(kFmt, kBM, kHeadDim, 1);
+      constexpr uint32_t kIdescPV = umma_idesc_f16(kFmt, kBM, D, 1);
       const uint32_t q_addr = smem_u32(q_smem);
       const uint32_t ring_addr = smem_u32(ring);
       bool ok = mbar_wait(&sb->q_full, 0, guard) && mbar_wait(&sb->kv_full[0], 0, guard);
@@ -306,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = 0; t < kQTiles; ++t) {
           if (n_kv_tile[t] == 0) continue;
 #pragma unroll
-          for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+          for (int kk = 0; kk < D / 16; ++kk) {
             umma_ss_elect(tmem + t * 128, kmajor_desc(q_addr + t * kTileBytes, kk),
                           kmajor_desc(ring_addr, kk), kIdescQK, kk > 0);
           }
@@ -357,7 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               k_ready = true;
             }
 #pragma unroll
-            for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+            for (int kk = 0; kk < D / 16; ++kk) {
               umma_ss_elect(tmem + t * 128, kmajor_desc(q_addr + t * kTileBytes, kk),
                             kmajor_desc(k_addr, kk), kIdescQK, kk > 0);
             }
@@ -447,7 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // j-1 (its completion is covered by s_full) and PV of tile j waits for the first P half,
         // so O is rescaled in place here, 16 columns at a time to keep registers for the scores.
 #pragma unroll 1
-        for (int c = 0; c < 8; ++c) {
+        for (int c = 0; c < D / 16; ++c) {
           uint32_t ov[16];
           tmem_ld16(taddr_o + c * 16, ov);
           tmem_ld_wait();
@@ -486,7 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 static_cast<int64_t>(row) * a.o_seq_stride +
                 static_cast<int64_t>(h) * a.o_head_stride;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < D / 32; ++c) {
         uint32_t ov[32];
         if (n_kv_t > 0) {
           tmem_ld32(taddr_o + c * 32, ov);
@@ -520,19 +532,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // One shared-memory opt-in per (kernel instantiation, device) and host thread.
-template <typename T, int kPoly, int kChunks>
+template <typename T, int D, int kPoly, int kChunks>
 int launch_variant(const PrefillArgs& a, const CUtensorMap& tmq, const CUtensorMap& tmk,
                    const CUtensorMap& tmv, int grid, int dev, cudaStream_t stream) {
+  constexpr int kSmemBytes = Geometry<D>::kSmemBytes;
   static thread_local int configured_device = -1;
   if (configured_device != dev) {
-    if (int st = check_cuda(cudaFuncSetAttribute(prefill_kernel<T, kPoly, kChunks>,
+    if (int st = check_cuda(cudaFuncSetAttribute(prefill_kernel<T, D, kPoly, kChunks>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  kSmemBytes),
                             "cudaFuncSetAttribute(prefill)"))
       return st;
     configured_device = dev;
   }
-  prefill_kernel<T, kPoly, kChunks><<<grid, kThreads, kSmemBytes, stream>>>(a, tmq, tmk, tmv);
+  prefill_kernel<T, D, kPoly, kChunks><<<grid, kThreads, kSmemBytes, stream>>>(a, tmq, tmk, tmv);
   return check_cuda(cudaGetLastError(), "prefill_kernel launch");
 }
 
@@ -559,16 +572,21 @@ template <typename T, int kChunks>
 int launch_poly(const PrefillArgs& a, const CUtensorMap& tmq, const CUtensorMap& tmk,
                 const CUtensorMap& tmv, int grid, int dev, cudaStream_t stream) {
   switch (poly_pairs()) {
-    case 0: return launch_variant<T, 0, kChunks>(a, tmq, tmk, tmv, grid, dev, stream);
-    case 2: return launch_variant<T, 2, kChunks>(a, tmq, tmk, tmv, grid, dev, stream);
-    case 3: return launch_variant<T, 3, kChunks>(a, tmq, tmk, tmv, grid, dev, stream);
-    default: return launch_variant<T, 4, kChunks>(a, tmq, tmk, tmv, grid, dev, stream);
+    case 0: return launch_variant<T, 128, 0, kChunks>(a, tmq, tmk, tmv, grid, dev, stream);
+    case 2: return launch_variant<T, 128, 2, kChunks>(a, tmq, tmk, tmv, grid, dev, stream);
+    case 3: return launch_variant<T, 128, 3, kChunks>(a, tmq, tmk, tmv, grid, dev, stream);
+    default: return launch_variant<T, 128, 4, kChunks>(a, tmq, tmk, tmv, grid, dev, stream);
   }
 }
 
+// head_dim 128 takes the tuning knobs; head_dim 64 runs the default variant.
 template <typename T>
 int launch_prefill(const PrefillArgs& a, const CUtensorMap& tmq, const CUtensorMap& tmk,
-                   const CUtensorMap& tmv, int grid, int dev, cudaStream_t stream) {
+                   const CUtensorMap& tmv, int head_dim, int grid, int dev, cudaStream_t stream) {
+  if (head_dim == 64) {
+    return launch_variant<T, 64, kDefaultPolyPairs, kDefaultPChunks>(a, tmq, tmk, tmv, grid, dev,
+                                                                     stream);
+  }
   if (p_chunks() == 1) return launch_poly<T, 1>(a, tmq, tmk, tmv, grid, dev, stream);
   return launch_poly<T, 2>(a, tmq, tmk, tmv, grid, dev, stream);
 }
@@ -586,8 +604,8 @@ int validate(const flb_attn_params* p) {
                 p->heads_kv);
   if (p->dtype != FLB_BF16 && p->dtype != FLB_FP16)
     return fail(FLB_ERR_UNSUPPORTED, "prefill takes bf16 or fp16 (dtype code %d)", p->dtype);
-  if (p->head_dim != kHeadDim)
-    return fail(FLB_ERR_UNSUPPORTED, "unsupported head_dim %d (this build: 128)", p->head_dim);
+  if (p->head_dim != 64 && p->head_dim != 128)
+    return fail(FLB_ERR_UNSUPPORTED, "unsupported head_dim %d (64 or 128)", p->head_dim);
   if (!(p->softmax_scale > 0.f))
     return fail(FLB_ERR_INVALID_ARGUMENT, "softmax_scale must be positive");
   const int64_t q_blocks = (p->seqlen_q + kRowsPerCta - 1) / kRowsPerCta;
@@ -650,6 +668,7 @@ extern "C" int flb_prefill_fwd(const flb_attn_params* p, flb_stream_t stream_) {
 
   const int grid = a.q_blocks * p->batch * p->heads;
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
-  if (p->dtype == FLB_BF16) return launch_prefill<__nv_bfloat16>(a, tmq, tmk, tmv, grid, dev, stream);
-  return launch_prefill<__half>(a, tmq, tmk, tmv, grid, dev, stream);
+  if (p->dtype == FLB_BF16)
+    return launch_prefill<__nv_bfloat16>(a, tmq, tmk, tmv, p->head_dim, grid, dev, stream);
+  return launch_prefill<__half>(a, tmq, tmk, tmv, p->head_dim, grid, dev, stream);
 }

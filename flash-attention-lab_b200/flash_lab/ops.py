@@ -81,8 +81,9 @@ class DecodeImpl:
 
 _HALF = (torch.bfloat16, torch.float16)
 PREFILL_IMPLS: dict[str, PrefillImpl] = {
-    "sm100": PrefillImpl(op="attention_sm100", dtypes=_HALF, head_dims=(128,)),
-    "mma_pipelined": PrefillImpl(op="attention_mma_pipelined", dtypes=_HALF, head_dims=(128,)),
+    "sm100": PrefillImpl(op="attention_sm100", dtypes=_HALF, head_dims=(64, 128)),
+    "mma_pipelined": PrefillImpl(op="attention_mma_pipelined", dtypes=_HALF,
+                                 head_dims=(64, 128)),
 }
 DECODE_IMPLS: dict[str, DecodeImpl] = {
     "splitkv": DecodeImpl(op="decode_splitkv", dtypes=_HALF, head_dims=(64, 128)),

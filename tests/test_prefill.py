@@ -32,6 +32,17 @@ SHAPES = [
     (1, 600, 129, 2, 1, 128),   # causal: whole CTAs without keys
 ]
 
+# head_dim 64 (the reference's other prefill head dim; Llama-3.2-1B's attention)
+SHAPES_D64 = [
+    (1, 1, 1, 1, 1, 64),
+    (3, 63, 63, 8, 2, 64),
+    (3, 257, 257, 8, 8, 64),
+    (2, 1024, 1024, 4, 4, 64),
+    (2, 37, 101, 4, 2, 64),
+    (1, 101, 37, 4, 4, 64),
+    (1, 600, 129, 2, 1, 64),
+]
+
 
 def make_inputs(shape, dtype, scale=1.0, seed=0):
     batch, seqlen_q, seqlen_k, heads, heads_kv, head_dim = shape
@@ -46,7 +57,7 @@ def make_inputs(shape, dtype, scale=1.0, seed=0):
 
 
 @pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
-@pytest.mark.parametrize("shape", SHAPES, ids=str)
+@pytest.mark.parametrize("shape", SHAPES + SHAPES_D64, ids=str)
 @pytest.mark.parametrize("dtype", DTYPES, ids=lambda d: str(d).removeprefix("torch."))
 def test_matches_oracle(dtype, shape, causal):
     q, k, v = make_inputs(shape, dtype)
@@ -62,11 +73,10 @@ def test_impl_names_run_the_same_kernel(impl):
     assert torch.equal(flash_lab.attention(q, k, v, causal=True), ref)   # auto
 
 
-GOLDEN_D128 = sorted(n for n, m in manifest().items()
-                     if m["kind"] == "prefill" and m["shape"][-1] == 128)
+GOLDEN_PREFILL = sorted(n for n, m in manifest().items() if m["kind"] == "prefill")
 
 
-@pytest.mark.parametrize("name", GOLDEN_D128)
+@pytest.mark.parametrize("name", GOLDEN_PREFILL)
 def test_matches_reference_goldens(name):
     """The reference's own fp64 outputs on the committed inputs (bf16 bits)."""
     g = load(name)
@@ -85,9 +95,10 @@ def test_matches_reference_goldens(name):
             assert np.abs(got[fin] - ref_lse[fin]).max() < 2e-3
 
 
-def test_large_scores():
+@pytest.mark.parametrize("head_dim", [64, 128])
+def test_large_scores(head_dim):
     # Scores of order 100 overflow exp() unless a running reference point is subtracted.
-    q, k, v = make_inputs((2, 129, 129, 4, 2, 128), torch.bfloat16, scale=10.0)
+    q, k, v = make_inputs((2, 129, 129, 4, 2, head_dim), torch.bfloat16, scale=10.0)
     out, lse = flash_lab.attention(q, k, v, causal=True, return_lse=True)
     check_prefill(out, lse, q, k, v, causal=True)
 
@@ -148,6 +159,17 @@ def test_baseline_config_sampled_rows(causal):
     q, k, v = make_inputs((4, 4096, 4096, 32, 32, 128), torch.bfloat16, seed=1)
     out, lse = flash_lab.attention(q, k, v, causal=causal, return_lse=True)
     gen = torch.Generator().manual_seed(5)
+    middle = torch.randperm(4094, generator=gen)[:254] + 1
+    rows = torch.cat([torch.tensor([0, 4095]), middle]).sort().values
+    check_prefill(out, lse, q, k, v, causal, rows=rows)
+
+
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+def test_head_dim_64_long_gqa_sampled_rows(causal):
+    """Llama-3.2-1B attention shape (H=32, H_kv=8, D=64) at 4096 tokens, on 256 sampled rows."""
+    q, k, v = make_inputs((2, 4096, 4096, 32, 8, 64), torch.bfloat16, seed=2)
+    out, lse = flash_lab.attention(q, k, v, causal=causal, return_lse=True)
+    gen = torch.Generator().manual_seed(6)
     middle = torch.randperm(4094, generator=gen)[:254] + 1
     rows = torch.cat([torch.tensor([0, 4095]), middle]).sort().values
     check_prefill(out, lse, q, k, v, causal, rows=rows)
