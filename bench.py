@@ -389,6 +389,14 @@ def run_extra(torch, flash_lab, device, dist, world, rank, args, peaks, traffic)
     del q, k, v
 
     l2_flush = torch.empty(512 * 2**20, dtype=torch.uint8, device=device)
+    l2_drain = torch.zeros(128 * 2**20, dtype=torch.float32, device=device)   # 512 MB
+
+    def flush_l2():
+        # Write a 512 MB buffer (4x L2), then read another: the written lines are dirty, and
+        # without the read pass their write-back would land inside the next timed call.
+        l2_flush.zero_()
+        l2_drain.sum()
+
     for name, (bb, hh, hk, lens_kind) in {
         "decode_mha_32k": (8, 32, 32, "full"),
         "decode_gqa_32k": (8, 32, 8, "ragged"),
@@ -409,7 +417,7 @@ def run_extra(torch, flash_lab, device, dist, world, rank, args, peaks, traffic)
         # Kernel-only time with L2 flushed before every call (flush outside the events).
         times = []
         for i in range(args.warmup + args.steps):
-            l2_flush.zero_()
+            flush_l2()
             st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             st.record()
             flash_lab.decode(qd, kc, vc, seq_lens)
@@ -427,13 +435,16 @@ def run_extra(torch, flash_lab, device, dist, world, rank, args, peaks, traffic)
                      "bytes_per_call": nbytes, "roofline_frac": gbs / peaks["hbm_gbs"],
                      "peak_gbs": peaks["hbm_gbs"], "config": f"B={bb} H={hh} H_kv={hk} "
                      f"S_max=32768 D=128 lengths={'32768' if lens_kind == 'full' else lens}",
-                     "l2": "512 MB buffer zeroed before every call (outside the events)"}
+                     "l2": "512 MB buffer written, then another 512 MB read, before every "
+                           "call (outside the events)"}
         del qd, kc, vc
 
-    # B=1 MHA at 32K with the KV sequence split across the ranks (decode_sharded: per-rank
-    # partials, NCCL all_gather, fixed-order merge); on one rank it is the plain split decode.
+    # B=1 MHA at 32K with the KV sequence split across the ranks. decode_b1_split: the peer
+    # exchange (each rank's split kernel pushes its partials into every rank's buffer over
+    # NVLink, then a bounded device wait and the fixed-order merge). decode_b1_split_allgather:
+    # per-rank partials, NCCL all_gather, merge. On one rank both are the plain split decode.
     from flash_lab import _capi
-    from flash_lab.distributed import ShardSpec, decode_sharded
+    from flash_lab.distributed import PeerExchange, ShardSpec, decode_sharded
 
     smax, hh, hk = 32768, 32, 32
     shard = ShardSpec.even(smax, world, rank)
@@ -447,31 +458,52 @@ def run_extra(torch, flash_lab, device, dist, world, rank, args, peaks, traffic)
     seq_lens = torch.full((1,), smax, device=device, dtype=torch.int32)
     sm = torch.cuda.get_device_properties(device).multi_processor_count
     splits = _capi.load().flb_decode_num_splits(1, hh, hk, d, shard.length, sm)
-    times = []
-    for i in range(args.warmup + args.steps):
-        l2_flush.zero_()
-        if dist is not None:
-            dist.barrier()
-        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        st.record()
-        decode_sharded(qd, k_shard, v_shard, seq_lens, shard, splits_per_rank=splits)
-        en.record()
-        if i >= args.warmup:
-            times.append((st, en))
-    torch.cuda.synchronize(device)
-    ms = statistics.median(a.elapsed_time(b) for a, b in times)
-    if dist is not None:
-        t = torch.tensor([ms], device=device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
     nbytes = decode_bytes(hh, hk, d, [smax], 1)
-    gbs = nbytes / (ms * 1e-3) / 1e9
-    out["decode_b1_split"] = {
-        "value": gbs, "unit": "GB/s", "ms_per_step": ms, "bytes_per_call": nbytes,
-        "per_gpu_roofline_frac": gbs / world / peaks["hbm_gbs"], "scaling": "strong",
-        "config": f"B=1 H=H_kv=32 D=128 32K keys split over {world} GPU(s), {splits} splits "
-                  f"per GPU, partials all-gathered over NCCL and merged in a fixed order",
-        "l2": "512 MB buffer zeroed before every call (outside the events)"}
+    # On one rank there is nothing to exchange: both lines time the local partials + merge.
+    exchange = PeerExchange(1, hh, d, splits_per_rank=splits) if world > 1 else None
+    try:
+        for name, ex, how in (("decode_b1_split", exchange, "partials pushed into every rank's "
+                               "buffer over NVLink peer memory, bounded device wait, merge"
+                               if world > 1 else "local partials and merge"),
+                              ("decode_b1_split_allgather", None, "partials all-gathered over "
+                               "NCCL, merge" if world > 1 else "local partials and merge")):
+            times = []
+            tick = torch.zeros(1, device=device)
+            for i in range(args.warmup + args.steps):
+                flush_l2()
+                if dist is not None:
+                    # Device-side rendezvous: the ranks' streams leave the all_reduce together,
+                    # so host launch skew stays out of the time.
+                    dist.all_reduce(tick)
+                # ~100 us of device sleep: the host enqueues the whole call before the start
+                # event fires, so the events time the device work, not Python launch overhead.
+                torch.cuda._sleep(200_000)
+                st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                st.record()
+                decode_sharded(qd, k_shard, v_shard, seq_lens, shard, splits_per_rank=splits,
+                               exchange=ex)
+                en.record()
+                if i >= args.warmup:
+                    times.append((st, en))
+            torch.cuda.synchronize(device)
+            ms = statistics.median(a.elapsed_time(b) for a, b in times)
+            if dist is not None:
+                t = torch.tensor([ms], device=device, dtype=torch.float64)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                ms = float(t.item())
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            out[name] = {
+                "value": gbs, "unit": "GB/s", "ms_per_step": ms, "bytes_per_call": nbytes,
+                "per_gpu_roofline_frac": gbs / world / peaks["hbm_gbs"], "scaling": "strong",
+                "config": f"B=1 H=H_kv=32 D=128 32K keys split over {world} GPU(s), {splits} "
+                          f"splits per GPU, {how} in a fixed order",
+                "l2": "512 MB buffer written, then another 512 MB read, before every call "
+                      "(outside the events)"}
+        if exchange is not None and exchange.read_status() != 0:
+            raise RuntimeError("a peer-exchange wait timed out during the bench")
+    finally:
+        if exchange is not None:
+            exchange.close()
     return out
 
 

@@ -40,14 +40,22 @@ constexpr int kDecodeConsumerWarps = 4;             // 16 keys of each tile per 
 constexpr int kDecodeThreads = (kDecodeConsumerWarps + 1) * 32;
 constexpr int kMaxHeadsPerCta = 16;                 // M of the warp MMA
 constexpr int kMaxSplits = 256;
+constexpr int kMaxDest = FLB_MAX_PEERS;             // destinations of pushed partials
 
 struct DecodeArgs {
   const void* q;
   void* o;
   float* lse;
   const int* seq_lens;
-  float* partial_o;   // [B, H, num_splits_total, D] when writing partials
-  float* partial_ml;  // [B, H, num_splits_total, 2]
+  // Split partials go to n_dest copies of [B, H, splits_total, D] / [B, H, splits_total, 2]
+  // (one unless they are pushed to every rank of a peer exchange). When arrive[0] is set, the
+  // launch adds 1 to every *arrive[i] (release, system scope) once all its partials are written;
+  // cta_done counts the CTAs that have finished (the last one publishes and resets it).
+  int n_dest;
+  float* partial_o[kMaxDest];
+  float* partial_ml[kMaxDest];
+  unsigned long long* arrive[kMaxDest];
+  unsigned int* cta_done;
   int* status;
   int64_t q_batch_stride, q_head_stride;
   int64_t o_batch_stride, o_head_stride;
@@ -85,6 +93,23 @@ __device__ __forceinline__ void load_kv_tile(uint8_t* dst, const CUtensorMap* ma
   for (int box = 0; box < boxes; ++box) {
     tma_load_4d(dst + box * (kDecodeBK * 128), map, bar, box * 64, tma_c(c, 1, key, hkv, b),
                 tma_c(c, 2, key, hkv, b), tma_c(c, 3, key, hkv, b));
+  }
+}
+
+// Publishes a push once per launch (called by one thread per CTA after the CTA's partial stores,
+// which a CTA barrier orders before it): each CTA fences at GPU scope and counts itself; the last
+// CTA to finish, having observed every count, fences at system scope and adds one arrival
+// (release, system scope) to every destination's counter, which makes all the launch's stores,
+// local or over NVLink, visible to a rank that acquires the counter. It then resets the count
+// for the next launch (launches on one stream do not overlap). A contended system-scope atomic
+// per CTA cost tens of microseconds, a system-scope fence per CTA about ten.
+__device__ __forceinline__ void publish_push(const DecodeArgs& a) {
+  __threadfence();
+  const unsigned int total = gridDim.x * gridDim.y;
+  if (atomicAdd(a.cta_done, 1u) == total - 1) {
+    __threadfence_system();
+    *a.cta_done = 0u;
+    for (int dst = 0; dst < a.n_dest; ++dst) red_release_sys_add(a.arrive[dst], 1ull);
   }
 }
 
@@ -309,7 +334,12 @@ __global__ void __launch_bounds__(kDecodeThreads)
   // All consumer warps are past the ring (the producer waited for its last copies), so the ring
   // memory is reused for the cross-warp merge.
   asm volatile("bar.sync 1, %0;" ::"n"(kDecodeConsumerWarps * 32) : "memory");
-  if (!ok || *abort_flag) return;
+  if (!ok || *abort_flag) {
+    // A CTA that gave up still counts itself in a push, so the counters stay consistent for the
+    // next step; the status word already tells the host this step's outputs are invalid.
+    if (a.write_partials && a.arrive[0] != nullptr && threadIdx.x == 0) publish_push(a);
+    return;
+  }
   float* wm = reinterpret_cast<float*>(smem);                         // [warps][16]
   float* wl = wm + kDecodeConsumerWarps * kMaxHeadsPerCta;            // [warps][16]
   float* wo = wl + kDecodeConsumerWarps * kMaxHeadsPerCta;            // [warps][16][D]
@@ -367,39 +397,79 @@ __global__ void __launch_bounds__(kDecodeThreads)
     } else {
       const int64_t slot =
           (static_cast<int64_t>(b) * a.heads + h) * a.splits_total + a.split_offset + split;
-      a.partial_o[slot * D + d] = num;
-      if (d == 0) {
-        a.partial_ml[2 * slot] = m;
-        a.partial_ml[2 * slot + 1] = den;
+      for (int dst = 0; dst < a.n_dest; ++dst) {
+        a.partial_o[dst][slot * D + d] = num;
+        if (d == 0) {
+          a.partial_ml[dst][2 * slot] = m;
+          a.partial_ml[dst][2 * slot + 1] = den;
+        }
       }
     }
   }
+  if (a.write_partials && a.arrive[0] != nullptr) {
+    asm volatile("bar.sync 1, %0;" ::"n"(kDecodeConsumerWarps * 32) : "memory");
+    if (tid == 0) publish_push(a);
+  }
 }
+
+// Arrivals a merge waits for: counters[src] >= expected for every source rank (null = none).
+struct PeerWait {
+  const unsigned long long* counters;
+  int world;
+  unsigned long long expected;
+  int64_t timeout_ns;
+  int* status;
+};
 
 // Fixed-order merge of the split partials of one (b, h): thread d owns output column d.
 // m = max_s m_s; l = sum_s l_s 2^(m_s - m); o = sum_s o_s 2^(m_s - m) / l (empty splits skipped).
-template <typename T>
+// kPeers: the partials are written by other GPUs; thread 0 first waits (bounded) for every
+// source's arrival counter, and the partials are read through L2 (ld.global.cg).
+template <typename T, bool kPeers>
 __global__ void decode_merge_kernel(const float* __restrict__ partial_o,
                                     const float* __restrict__ partial_ml, int heads, int head_dim,
                                     int num_splits, T* o, int64_t o_batch_stride,
-                                    int64_t o_head_stride, float* lse) {
+                                    int64_t o_head_stride, float* lse, PeerWait wait) {
   // Launched as a programmatic dependent of the split kernel: wait for its writes first (a no-op
   // when launched normally).
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  if constexpr (kPeers) {
+    __shared__ int s_failed;
+    if (threadIdx.x == 0) {
+      int failed = 0;
+      const uint64_t start = global_timer_ns();
+      for (int src = 0; src < wait.world && !failed; ++src) {
+        uint32_t polls = 0;
+        while (ld_acquire_sys_u64(wait.counters + src) < wait.expected) {
+          __nanosleep(64);
+          if (((++polls) & 15u) == 0 &&
+              global_timer_ns() - start > static_cast<uint64_t>(wait.timeout_ns)) {
+            failed = 1;
+            if (wait.status != nullptr) atomicCAS(wait.status, 0, kDevPeerTimeout);
+            break;
+          }
+        }
+      }
+      s_failed = failed;
+    }
+    __syncthreads();
+    if (s_failed) return;
+  }
+  auto load = [](const float* p) { return kPeers ? __ldcg(p) : *p; };
   const int bh = blockIdx.x;
   const int b = bh / heads;
   const int h = bh - b * heads;
   const int64_t base = static_cast<int64_t>(bh) * num_splits;
   float m = -INFINITY;
-  for (int s = 0; s < num_splits; ++s) m = fmaxf(m, partial_ml[2 * (base + s)]);
+  for (int s = 0; s < num_splits; ++s) m = fmaxf(m, load(partial_ml + 2 * (base + s)));
   for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
     float num = 0.f, den = 0.f;
     for (int s = 0; s < num_splits; ++s) {
-      const float ms = partial_ml[2 * (base + s)];
+      const float ms = load(partial_ml + 2 * (base + s));
       if (ms != -INFINITY) {
         const float f = ex2(ms - m);
-        num += partial_o[(base + s) * head_dim + d] * f;
-        den += partial_ml[2 * (base + s) + 1] * f;
+        num += load(partial_o + (base + s) * head_dim + d) * f;
+        den += load(partial_ml + 2 * (base + s) + 1) * f;
       }
     }
     const float val = den > 0.f ? num / den : 0.f;
@@ -433,9 +503,10 @@ int launch_split(const DecodeArgs& args, const CUtensorMap& tmk, const CUtensorM
   return check_cuda(cudaGetLastError(), "decode_split_kernel launch");
 }
 
-template <typename T>
+template <typename T, bool kPeers = false>
 int launch_merge(const float* po, const float* pml, int batch, int heads, int head_dim,
-                 int splits, void* o, int64_t obs, int64_t ohs, float* lse, cudaStream_t stream) {
+                 int splits, void* o, int64_t obs, int64_t ohs, float* lse, cudaStream_t stream,
+                 PeerWait wait = PeerWait{}) {
   // Programmatic dependent launch: the merge grid is scheduled while the split kernel drains
   // and waits (griddepcontrol.wait) for its results, which hides the launch gap between them.
   cudaLaunchConfig_t cfg = {};
@@ -449,8 +520,8 @@ int launch_merge(const float* po, const float* pml, int batch, int heads, int he
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   T* out = static_cast<T*>(o);
-  return check_cuda(cudaLaunchKernelEx(&cfg, decode_merge_kernel<T>, po, pml, heads, head_dim,
-                                       splits, out, obs, ohs, lse),
+  return check_cuda(cudaLaunchKernelEx(&cfg, decode_merge_kernel<T, kPeers>, po, pml, heads,
+                                       head_dim, splits, out, obs, ohs, lse, wait),
                     "decode_merge_kernel launch");
 }
 
@@ -531,29 +602,23 @@ int dispatch(int dtype, int head_dim, F&& f) {
   return f(__half{}, std::integral_constant<int, 64>{});
 }
 
+// Split count from shapes only (so a captured CUDA graph stays valid for any lengths). Measured
+// on B200 at 32K keys: about one CTA per SM is best (B=1 MHA: 4 splits 89 us against 107 us for
+// 37; B=8 MHA: 1 split 606 us against 626 us for 8; B=8 GQA with ragged lengths: 3 splits
+// 124 us against 132 us for 18), and splits shorter than 8 tiles (512 keys) lose to their fixed
+// costs. More, shorter CTAs pay more prologues, more partials and a longer merge than the load
+// balance they buy.
 int splits_for(int batch, int heads, int heads_kv, int head_dim, int max_seqlen, int sm_count) {
+  (void)head_dim;
   if (batch <= 0 || heads <= 0 || heads_kv <= 0 || heads % heads_kv != 0 || max_seqlen <= 0 ||
       sm_count <= 0)
     return 1;
   const int group = heads / heads_kv;
   const int chunks = (group + kMaxHeadsPerCta - 1) / kMaxHeadsPerCta;
   const int64_t ctas = static_cast<int64_t>(batch) * heads_kv * chunks;
-  const int per_sm = head_dim == 128 ? 2 : 3;  // resident CTAs per SM for the ring size
-  const int64_t slots = static_cast<int64_t>(sm_count) * per_sm;
-  // At least 4 tiles per split of the longest sequence.
-  const int max_splits =
-      static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(kMaxSplits, max_seqlen / 256)));
-  if (ctas >= 4 * slots) return 1;
-  // Smallest split count giving >= 3 waves with a full-enough last wave; else about 4 waves.
-  // (Targeting 6 waves measured slower: more partials to merge and more CTA prologues.)
-  for (int s = 1; s <= max_splits; ++s) {
-    const double waves = static_cast<double>(ctas * s) / static_cast<double>(slots);
-    if (waves < 3.0) continue;
-    const double eff = waves / std::ceil(waves);
-    if (eff >= 0.9) return s;
-  }
-  const int64_t want = (4 * slots + ctas - 1) / ctas;
-  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(max_splits, want)));
+  const int64_t by_sm = (sm_count + ctas - 1) / ctas;
+  const int64_t by_len = std::max<int64_t>(1, max_seqlen / (8 * kDecodeBK));
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({by_sm, by_len, kMaxSplits})));
 }
 
 }  // namespace
@@ -610,15 +675,16 @@ extern "C" int flb_decode_fwd(const flb_decode_params* p, flb_stream_t stream_) 
   if (reinterpret_cast<uintptr_t>(p->workspace) % 256 != 0)
     return fail(FLB_ERR_MISALIGNED, "workspace must be 256-byte aligned");
   const size_t slots = static_cast<size_t>(p->batch) * p->heads * splits;
-  a.partial_o = static_cast<float*>(p->workspace);
-  a.partial_ml = reinterpret_cast<float*>(static_cast<char*>(p->workspace) +
-                                          (slots * p->head_dim * sizeof(float) + 255) / 256 * 256);
+  a.n_dest = 1;
+  a.partial_o[0] = static_cast<float*>(p->workspace);
+  a.partial_ml[0] = reinterpret_cast<float*>(
+      static_cast<char*>(p->workspace) + (slots * p->head_dim * sizeof(float) + 255) / 256 * 256);
   a.write_partials = 1;
   return dispatch(p->dtype, p->head_dim, [&](auto tag, auto dim) {
     using T = decltype(tag);
     if (int st = launch_split<T, decltype(dim)::value>(a, tmk, tmv, splits, grid_y, stream))
       return st;
-    return launch_merge<T>(a.partial_o, a.partial_ml, p->batch, p->heads, p->head_dim, splits,
+    return launch_merge<T>(a.partial_o[0], a.partial_ml[0], p->batch, p->heads, p->head_dim, splits,
                            p->o, p->o_batch_stride, p->o_head_stride, p->lse, stream);
   });
 }
@@ -652,8 +718,9 @@ extern "C" int flb_decode_partials(const flb_decode_params* p, int32_t key_begin
   a.split_offset = 0;
   a.splits_total = q.num_splits;
   a.write_partials = 1;
-  a.partial_o = partial_o;
-  a.partial_ml = partial_ml;
+  a.n_dest = 1;
+  a.partial_o[0] = partial_o;
+  a.partial_ml[0] = partial_ml;
   const int grid_y = q.batch * q.heads_kv * a.head_chunks;
   if (grid_y > 65535)
     return fail(FLB_ERR_UNSUPPORTED, "batch * heads_kv * head chunks = %d exceeds 65535", grid_y);
@@ -680,5 +747,135 @@ extern "C" int flb_decode_merge(const float* partial_o, const float* partial_ml,
   if (dtype == FLB_FP16)
     return launch_merge<__half>(partial_o, partial_ml, batch, heads, head_dim, num_splits, o,
                                 o_batch_stride, o_head_stride, lse, stream);
+  return fail(FLB_ERR_UNSUPPORTED, "merge takes bf16 or fp16");
+}
+
+// ---------------------------------------------------------------------------------------------
+// Cross-GPU exchange over peer memory (layout in include/flash_lab_b200.h).
+// ---------------------------------------------------------------------------------------------
+namespace flb {
+namespace {
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+struct ExchangeLayout {
+  size_t counters;      // bytes of the counter block
+  size_t po_bytes;      // partial_o of one parity region
+  size_t region;        // one parity region
+};
+
+ExchangeLayout exchange_layout(int world, int batch, int heads, int head_dim, int splits) {
+  ExchangeLayout l;
+  // world arrival counters, then this rank's CTA count of the current push.
+  l.counters = align256(static_cast<size_t>(world + 1) * sizeof(unsigned long long));
+  const size_t slots = static_cast<size_t>(batch) * heads * world * splits;
+  l.po_bytes = align256(slots * head_dim * sizeof(float));
+  l.region = align256(l.po_bytes + slots * 2 * sizeof(float));
+  return l;
+}
+
+int check_exchange(const flb_peer_exchange* x) {
+  if (x == nullptr) return fail(FLB_ERR_INVALID_ARGUMENT, "exchange is NULL");
+  if (x->world < 1 || x->world > FLB_MAX_PEERS || x->rank < 0 || x->rank >= x->world)
+    return fail(FLB_ERR_INVALID_ARGUMENT, "exchange: rank %d of world %d (at most %d ranks)",
+                x->rank, x->world, FLB_MAX_PEERS);
+  for (int r = 0; r < x->world; ++r) {
+    if (x->buffers[r] == nullptr)
+      return fail(FLB_ERR_INVALID_ARGUMENT, "exchange: buffer of rank %d is NULL", r);
+    if (reinterpret_cast<uintptr_t>(x->buffers[r]) % 256 != 0)
+      return fail(FLB_ERR_MISALIGNED, "exchange: buffer of rank %d is not 256-byte aligned", r);
+  }
+  return FLB_OK;
+}
+
+}  // namespace
+}  // namespace flb
+
+extern "C" size_t flb_peer_exchange_bytes(int32_t world, int32_t batch, int32_t heads,
+                                          int32_t head_dim, int32_t splits_per_rank) {
+  if (world < 1 || batch <= 0 || heads <= 0 || head_dim <= 0 || splits_per_rank <= 0) return 0;
+  const ExchangeLayout l = exchange_layout(world, batch, heads, head_dim, splits_per_rank);
+  return l.counters + 2 * l.region;
+}
+
+extern "C" int flb_decode_partials_push(const flb_decode_params* p, int32_t key_begin,
+                                        int32_t key_end, const flb_peer_exchange* x,
+                                        int32_t parity, flb_stream_t stream_) {
+  clear_error();
+  if (p == nullptr) return fail(FLB_ERR_INVALID_ARGUMENT, "params is NULL");
+  if (int st = check_exchange(x)) return st;
+  flb_decode_params q = *p;
+  static char dummy;
+  if (q.o == nullptr) q.o = &dummy;
+  if (q.lse == nullptr) q.lse = reinterpret_cast<float*>(&dummy);
+  if (int st = validate(&q)) return st;
+  if (key_begin < 0 || key_end < key_begin)
+    return fail(FLB_ERR_INVALID_ARGUMENT, "bad key window [%d, %d)", key_begin, key_end);
+  if (q.num_splits < 1) return fail(FLB_ERR_INVALID_ARGUMENT, "num_splits must be >= 1 here");
+  if (parity != 0 && parity != 1) return fail(FLB_ERR_INVALID_ARGUMENT, "parity must be 0 or 1");
+  int dev = 0, sm_count = 0;
+  if (int st = current_device_info(&dev, &sm_count, nullptr, nullptr)) return st;
+  CUtensorMap tmk, tmv;
+  TmaCoords kc{}, vc{};
+  if (int st = build_maps(&q, &tmk, &tmv, &kc, &vc)) return st;
+  DecodeArgs a = make_args(&q);
+  a.kc = kc;
+  a.vc = vc;
+  a.key_begin = key_begin;
+  a.key_end = key_end;
+  a.num_splits = q.num_splits;
+  a.split_offset = x->rank * q.num_splits;
+  a.splits_total = x->world * q.num_splits;
+  a.write_partials = 1;
+  const ExchangeLayout l = exchange_layout(x->world, q.batch, q.heads, q.head_dim, q.num_splits);
+  a.n_dest = x->world;
+  for (int r = 0; r < x->world; ++r) {
+    char* region = static_cast<char*>(x->buffers[r]) + l.counters + parity * l.region;
+    a.partial_o[r] = reinterpret_cast<float*>(region);
+    a.partial_ml[r] = reinterpret_cast<float*>(region + l.po_bytes);
+    a.arrive[r] = static_cast<unsigned long long*>(x->buffers[r]) + x->rank;
+  }
+  a.cta_done = reinterpret_cast<unsigned int*>(
+      static_cast<unsigned long long*>(x->buffers[x->rank]) + x->world);
+  const int grid_y = q.batch * q.heads_kv * a.head_chunks;
+  if (grid_y > 65535)
+    return fail(FLB_ERR_UNSUPPORTED, "batch * heads_kv * head chunks = %d exceeds 65535", grid_y);
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  return dispatch(q.dtype, q.head_dim, [&](auto tag, auto dim) {
+    return launch_split<decltype(tag), decltype(dim)::value>(a, tmk, tmv, q.num_splits, grid_y,
+                                                             stream);
+  });
+}
+
+extern "C" int flb_decode_merge_peers(const flb_peer_exchange* x, int32_t parity,
+                                      uint64_t expected, int32_t batch, int32_t heads,
+                                      int32_t head_dim, int32_t splits_per_rank, int32_t dtype,
+                                      void* o, int64_t o_batch_stride, int64_t o_head_stride,
+                                      float* lse, int32_t* status, flb_stream_t stream_) {
+  clear_error();
+  if (int st = check_exchange(x)) return st;
+  if (!o || !lse) return fail(FLB_ERR_INVALID_ARGUMENT, "a required pointer is NULL");
+  if (batch <= 0 || heads <= 0 || splits_per_rank <= 0 || (head_dim != 64 && head_dim != 128))
+    return fail(FLB_ERR_INVALID_ARGUMENT, "bad merge shape");
+  if (parity != 0 && parity != 1) return fail(FLB_ERR_INVALID_ARGUMENT, "parity must be 0 or 1");
+  const ExchangeLayout l = exchange_layout(x->world, batch, heads, head_dim, splits_per_rank);
+  const char* region =
+      static_cast<const char*>(x->buffers[x->rank]) + l.counters + parity * l.region;
+  const float* po = reinterpret_cast<const float*>(region);
+  const float* pml = reinterpret_cast<const float*>(region + l.po_bytes);
+  PeerWait wait;
+  wait.counters = static_cast<const unsigned long long*>(x->buffers[x->rank]);
+  wait.world = x->world;
+  wait.expected = expected;
+  wait.timeout_ns = x->timeout_ns > 0 ? x->timeout_ns : static_cast<int64_t>(kWaitTimeoutNs);
+  wait.status = status;
+  const int splits = x->world * splits_per_rank;
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  if (dtype == FLB_BF16)
+    return launch_merge<__nv_bfloat16, true>(po, pml, batch, heads, head_dim, splits, o,
+                                             o_batch_stride, o_head_stride, lse, stream, wait);
+  if (dtype == FLB_FP16)
+    return launch_merge<__half, true>(po, pml, batch, heads, head_dim, splits, o,
+                                      o_batch_stride, o_head_stride, lse, stream, wait);
   return fail(FLB_ERR_UNSUPPORTED, "merge takes bf16 or fp16");
 }

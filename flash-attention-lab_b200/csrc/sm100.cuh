@@ -31,7 +31,20 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 enum DeviceStatus : int {
   kDevOk = 0,
   kDevWaitTimeout = 1,  // an mbarrier wait exceeded its deadline; outputs are invalid
+  kDevPeerTimeout = 2,  // another GPU's partials did not arrive in time; outputs are invalid
 };
+
+// System-scope release add (a counter another GPU polls) and acquire load (of a counter other
+// GPUs add to), for the cross-GPU decode exchange over NVLink peer memory.
+__device__ __forceinline__ void red_release_sys_add(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
 
 // One deadline for every wait of a launch: a healthy pipeline stage completes in microseconds.
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s

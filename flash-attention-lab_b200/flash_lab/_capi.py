@@ -26,6 +26,8 @@ FLB_ERR_NO_DEVICE = 6
 FLB_BF16 = 0
 FLB_FP16 = 1
 
+FLB_MAX_PEERS = 8
+
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _i32 = ctypes.c_int32
@@ -60,6 +62,14 @@ class DecodeParams(ctypes.Structure):
     ]
 
 
+class PeerExchange(ctypes.Structure):
+    _fields_ = [
+        ("world", _i32), ("rank", _i32),
+        ("buffers", _p * FLB_MAX_PEERS),
+        ("timeout_ns", _i64),
+    ]
+
+
 # Every symbol include/flash_lab_b200.h declares, with its ctypes signature.
 SIGNATURES = {
     "flb_version": ([], ctypes.c_int),
@@ -76,6 +86,16 @@ SIGNATURES = {
     "flb_selftest_umma": ([_p, _p, _p, _p, _p, _p, _p, _p], ctypes.c_int),
     "flb_decode_fwd_static": ([ctypes.POINTER(DecodeParams), _p], ctypes.c_int),
     "flb_decode_static_scratch_bytes": ([], ctypes.c_size_t),
+    "flb_peer_handle_bytes": ([], ctypes.c_size_t),
+    "flb_peer_alloc": ([ctypes.c_size_t, ctypes.POINTER(_p), _p], ctypes.c_int),
+    "flb_peer_open": ([_p, ctypes.POINTER(_p)], ctypes.c_int),
+    "flb_peer_close": ([_p], ctypes.c_int),
+    "flb_peer_free": ([_p], ctypes.c_int),
+    "flb_peer_exchange_bytes": ([_i32, _i32, _i32, _i32, _i32], ctypes.c_size_t),
+    "flb_decode_partials_push": ([ctypes.POINTER(DecodeParams), _i32, _i32,
+                                  ctypes.POINTER(PeerExchange), _i32, _p], ctypes.c_int),
+    "flb_decode_merge_peers": ([ctypes.POINTER(PeerExchange), _i32, ctypes.c_uint64, _i32, _i32,
+                                _i32, _i32, _i32, _p, _i64, _i64, _p, _p, _p], ctypes.c_int),
 }
 
 _LIB: ctypes.CDLL | None = None

@@ -19,6 +19,14 @@ length and the split count, and the merge order is fixed. The exchange moves
 B * H * splits_per_rank * (D + 2) * 4 bytes per rank: 16.6 KB at B=1, H=32, D=128, 1 split.
 There is no CPU path: the kernels are the library's, and only the collective is torch's.
 
+With a PeerExchange, phases 1 and 2 are one kernel: each rank's split kernel stores its partials
+straight into every rank's exchange buffer over NVLink (CUDA IPC peer mappings); its last CTA to
+finish then adds one arrival to this rank's counter in every buffer (release, system scope). Phase 3 waits on the
+device, bounded by a timeout, until every source's counter has reached the step's expected count,
+and merges; no NCCL call is on the path. Buffers alternate by step parity, so a rank that runs one
+step ahead cannot overwrite partials another rank is still merging. The result is bitwise equal
+to the all-gather path (same partials, same merge order).
+
 No counterpart in the reference, which is single-GPU (README.md:183 there); the merge follows
 its split merge (csrc/decode/decode.cu:204-228).
 """
@@ -114,16 +122,130 @@ def gather_in_rank_order(po: torch.Tensor, pml: torch.Tensor, group=None):
     return merged[..., :head_dim].contiguous(), merged[..., head_dim:].contiguous()
 
 
+class PeerExchange:
+    """Exchange buffers for decode_sharded over peer memory, one per (process group, shape).
+
+    Collective: every rank of `group` constructs it with the same shapes, with its own GPU
+    current. Each rank allocates one buffer (flb_peer_alloc), the CUDA IPC handles are
+    all-gathered over the process group once, and every rank maps the others' buffers. Not for
+    CUDA-graph capture: the expected arrival count is a host value that grows with every step.
+    """
+
+    def __init__(self, batch: int, heads: int, head_dim: int, splits_per_rank: int = 1,
+                 group=None, timeout_s: float = 2.0):
+        lib = _capi.load()
+        self._lib = lib
+        self.group = group
+        multi = dist.is_initialized() and dist.get_world_size(group) > 1
+        self.world = dist.get_world_size(group) if multi else 1
+        self.rank = dist.get_rank(group) if multi else 0
+        if self.world > _capi.FLB_MAX_PEERS:
+            raise ValueError(f"a peer exchange connects at most {_capi.FLB_MAX_PEERS} ranks, "
+                             f"got {self.world}")
+        self.shape = (batch, heads, head_dim, splits_per_rank)
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        nbytes = lib.flb_peer_exchange_bytes(self.world, batch, heads, head_dim, splits_per_rank)
+        if nbytes == 0:
+            raise ValueError(f"bad exchange shape {self.shape}")
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * lib.flb_peer_handle_bytes())()
+        rc = lib.flb_peer_alloc(nbytes, ctypes.byref(own), handle)
+        if rc != _capi.FLB_OK:
+            raise RuntimeError(f"flb_peer_alloc: {_capi.error_message(lib, rc)}")
+        self._own = own.value
+        handles = [bytes(handle)]
+        if multi:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+        x = _capi.PeerExchange()
+        x.world, x.rank, x.timeout_ns = self.world, self.rank, int(timeout_s * 1e9)
+        self._opened = []
+        for r in range(self.world):
+            if r == self.rank:
+                x.buffers[r] = self._own
+                continue
+            ptr = ctypes.c_void_p()
+            raw = (ctypes.c_ubyte * len(handles[r])).from_buffer_copy(handles[r])
+            rc = lib.flb_peer_open(raw, ctypes.byref(ptr))
+            if rc != _capi.FLB_OK:
+                raise RuntimeError(f"flb_peer_open(rank {r}): {_capi.error_message(lib, rc)}")
+            x.buffers[r] = ptr.value
+            self._opened.append(ptr.value)
+        self.x = x
+        self.steps = 0       # decode steps taken (selects the parity region)
+        self.expected = 0    # arrivals every source counter has reached after those steps
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def read_status(self) -> int:
+        """Device status of the exchange waits (0, or 2 when a peer's partials timed out);
+        synchronises and clears it."""
+        code = int(self.status.item())
+        self.status.zero_()
+        return code
+
+    def close(self) -> None:
+        """Collective: unmaps the peers' buffers and frees this rank's buffer."""
+        if self._own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)      # nobody still writes into a buffer being freed
+        for ptr in self._opened:
+            self._lib.flb_peer_close(ptr)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        self._lib.flb_peer_free(self._own)
+        self._own = None
+        self._opened = []
+
+
+def _decode_sharded_peer(q3, k_shard, v_shard, lens, splits, scale, exchange: PeerExchange):
+    lib = exchange._lib
+    batch, heads, head_dim = q3.shape
+    if exchange.shape != (batch, heads, head_dim, splits):
+        raise ValueError(f"the exchange was built for (batch, heads, head_dim, splits) = "
+                         f"{exchange.shape}, got {(batch, heads, head_dim, splits)}")
+    stream = torch.cuda.current_stream(q3.device).cuda_stream
+    p = _capi.DecodeParams(
+        q3.data_ptr(), k_shard.data_ptr(), v_shard.data_ptr(), 0, 0, lens.data_ptr(),
+        q3.stride(0), q3.stride(1),
+        k_shard.stride(0), k_shard.stride(1), k_shard.stride(2),
+        v_shard.stride(0), v_shard.stride(1), v_shard.stride(2),
+        0, 0,
+        batch, heads, k_shard.shape[2], head_dim, k_shard.shape[1], splits, _dtype_code(q3.dtype),
+        float(scale), 0, 0, exchange.status.data_ptr(),
+    )
+    parity = exchange.steps & 1
+    rc = lib.flb_decode_partials_push(ctypes.byref(p), 0, k_shard.shape[1],
+                                      ctypes.byref(exchange.x), parity, stream)
+    if rc != _capi.FLB_OK:
+        raise RuntimeError(f"flb_decode_partials_push: {_capi.error_message(lib, rc)}")
+    exchange.expected += 1
+    exchange.steps += 1
+    o = torch.empty((batch, heads, head_dim), device=q3.device, dtype=q3.dtype)
+    lse = torch.empty((batch, heads), device=q3.device, dtype=torch.float32)
+    rc = lib.flb_decode_merge_peers(ctypes.byref(exchange.x), parity, exchange.expected, batch,
+                                    heads, head_dim, splits, _dtype_code(q3.dtype), o.data_ptr(),
+                                    o.stride(0), o.stride(1), lse.data_ptr(),
+                                    exchange.status.data_ptr(), stream)
+    if rc != _capi.FLB_OK:
+        raise RuntimeError(f"flb_decode_merge_peers: {_capi.error_message(lib, rc)}")
+    return o, lse
+
+
 def decode_sharded(q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.Tensor,
                    seq_lens: torch.Tensor, shard: ShardSpec, splits_per_rank: int = 1,
                    softmax_scale: float | None = None, group=None, return_lse: bool = False,
+                   exchange: PeerExchange | None = None,
                    _partials=shard_partials, _merge=merge_partials):
     """One decode step over a KV cache split along the sequence across the ranks of `group`.
 
     q [B, H, D] or [B, 1, H, D] (identical on every rank); k_shard / v_shard
     [B, S_shard, H_kv, D] hold keys [shard.offset, shard.offset + shard.length) of every
     sequence; seq_lens [B] int32 are the global lengths. Returns o (q's shape) and, with
-    return_lse, the natural-log LSE [B, H], on every rank.
+    return_lse, the natural-log LSE [B, H], on every rank. With `exchange`, the partials move
+    over peer memory (one fused push kernel per rank) instead of an all_gather; a wait that
+    times out leaves code 2 in exchange.status (exchange.read_status()).
     """
     if splits_per_rank < 1:
         raise ValueError(f"splits_per_rank must be positive, got {splits_per_rank}")
@@ -133,6 +255,12 @@ def decode_sharded(q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.Tensor
     q3 = q[:, 0] if q.dim() == 4 else q
     scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(q3.shape[-1])
     lens = local_lengths(seq_lens, shard)
+    if exchange is not None:
+        o, lse = _decode_sharded_peer(q3, k_shard, v_shard, lens, splits_per_rank, scale,
+                                      exchange)
+        if q.dim() == 4:
+            o = o.unsqueeze(1)
+        return (o, lse) if return_lse else o
     po, pml = _partials(q3, k_shard, v_shard, lens, splits_per_rank, scale)
     if dist.is_initialized() and dist.get_world_size(group) > 1:
         po, pml = gather_in_rank_order(po, pml, group)

@@ -32,6 +32,9 @@ extern "C" {
 
 #define FLB_ABI_VERSION 1
 
+/* Most ranks a peer exchange (cross-GPU decode merge over NVLink) connects. */
+#define FLB_MAX_PEERS 8
+
 /* Stream handle: the same object as cudaStream_t / CUstream (NULL = legacy default stream). */
 typedef struct CUstream_st* flb_stream_t;
 
@@ -175,6 +178,64 @@ int flb_decode_merge(const float* partial_o, const float* partial_ml, int32_t ba
                      int32_t heads, int32_t head_dim, int32_t num_splits, int32_t dtype, void* o,
                      int64_t o_batch_stride, int64_t o_head_stride, float* lse,
                      flb_stream_t stream);
+
+/*
+ * Cross-GPU decode exchange over peer memory (one process per GPU, NVLink / NVSwitch). No
+ * counterpart in the reference, which is single-GPU: these replace an all-gather of the split
+ * partials (flb_decode_partials + a collective + flb_decode_merge) with stores straight into
+ * every rank's buffer and a bounded wait on arrival counters.
+ *
+ * Each rank allocates one exchange buffer with flb_peer_alloc, sends the handle to the other
+ * ranks (any host channel) and maps theirs with flb_peer_open. Buffer layout, for `world` ranks,
+ * B sequences, H query heads, head_dim D and S splits per rank (W*S splits in global order):
+ *   [0, 256 * ceil(8 (W + 1) / 256))  uint64 arrival counters, one per source rank, then the
+ *                                    CTA count of this rank's push in progress (all start at 0)
+ *   then two parity regions, each partial_o [B, H, W*S, D] fp32 (256-byte aligned) followed by
+ *   partial_ml [B, H, W*S, 2] fp32 (the flb_decode_partials layout).
+ * Step n of a decode uses parity n % 2, so a rank one step ahead never overwrites partials a
+ * slower rank is still merging.
+ */
+size_t flb_peer_handle_bytes(void);
+/* cudaMalloc + zero-fill + CUDA IPC export of `bytes` of device memory on the current device. */
+int flb_peer_alloc(size_t bytes, void** ptr, void* handle);
+/* Maps another process's buffer (its handle) into this process. */
+int flb_peer_open(const void* handle, void** ptr);
+int flb_peer_close(void* ptr);
+int flb_peer_free(void* ptr);
+
+typedef struct {
+  int32_t world;                   /* ranks, 1..FLB_MAX_PEERS */
+  int32_t rank;                    /* this rank */
+  void* buffers[FLB_MAX_PEERS];    /* every rank's exchange buffer as mapped here ([rank] = own) */
+  int64_t timeout_ns;              /* bound on the wait for the other ranks (<= 0: 2 s) */
+} flb_peer_exchange;
+
+/* Bytes of one exchange buffer for these shapes (the same on every rank). */
+size_t flb_peer_exchange_bytes(int32_t world, int32_t batch, int32_t heads, int32_t head_dim,
+                               int32_t splits_per_rank);
+
+/*
+ * This rank's split stage (flb_decode_partials on keys [key_begin, key_end) with
+ * params->num_splits splits) writing its partials at global split indices
+ * [rank * S, rank * S + S) of parity region `parity` in EVERY rank's buffer. Once all its CTAs
+ * have written, the launch adds 1, with release semantics at system scope, to counter [rank] of
+ * every buffer: after n pushes every counter a rank waits on reads n.
+ */
+int flb_decode_partials_push(const flb_decode_params* params, int32_t key_begin,
+                             int32_t key_end, const flb_peer_exchange* exchange, int32_t parity,
+                             flb_stream_t stream);
+
+/*
+ * Waits until every source counter of this rank's buffer has reached `expected` (bounded by
+ * exchange->timeout_ns; on expiry it writes code 2 to `status` and leaves o / lse unwritten),
+ * then merges the W*S partials of parity region `parity` in global split order, exactly as
+ * flb_decode_merge does.
+ */
+int flb_decode_merge_peers(const flb_peer_exchange* exchange, int32_t parity, uint64_t expected,
+                           int32_t batch, int32_t heads, int32_t head_dim,
+                           int32_t splits_per_rank, int32_t dtype, void* o,
+                           int64_t o_batch_stride, int64_t o_head_stride, float* lse,
+                           int32_t* status, flb_stream_t stream);
 
 /*
  * Unit test of the tcgen05 building blocks the prefill kernel uses (no reference counterpart;

@@ -60,7 +60,8 @@ def _c_layout(struct: str, fields: list[str], tmp_path) -> dict[str, int]:
 
 
 @pytest.mark.parametrize("struct,cls", [("flb_attn_params", _capi.AttnParams),
-                                        ("flb_decode_params", _capi.DecodeParams)])
+                                        ("flb_decode_params", _capi.DecodeParams),
+                                        ("flb_peer_exchange", _capi.PeerExchange)])
 def test_struct_layout_matches_header(struct, cls, tmp_path):
     fields = [name for name, _ in cls._fields_]
     layout = _c_layout(struct, fields, tmp_path)
@@ -92,3 +93,29 @@ def test_workspace_bytes(lib):
     n = lib.flb_decode_workspace_bytes(8, 32, 128, 16)
     slots = 8 * 32 * 16
     assert n >= slots * 128 * 4 + slots * 8
+
+
+def test_peer_exchange_sizes(lib):
+    # Layout: counters (world + 1 uint64 in a 256-byte block), then two parity regions of
+    # partial_o + partial_ml.
+    world, batch, heads, d, splits = 2, 1, 32, 128, 4
+    slots = batch * heads * world * splits
+    po = -(-slots * d * 4 // 256) * 256
+    region = -(-(po + slots * 2 * 4) // 256) * 256
+    assert lib.flb_peer_exchange_bytes(world, batch, heads, d, splits) == 256 + 2 * region
+    assert lib.flb_peer_exchange_bytes(0, batch, heads, d, splits) == 0
+    assert lib.flb_peer_handle_bytes() == 64
+
+
+def test_peer_exchange_host_validation(lib):
+    p = _capi.DecodeParams()
+    x = _capi.PeerExchange()
+    x.world, x.rank = 2, 0           # buffers left NULL
+    assert lib.flb_decode_partials_push(ctypes.byref(p), 0, 1, ctypes.byref(x), 0, None) \
+        == _capi.FLB_ERR_INVALID_ARGUMENT
+    assert b"buffer of rank 0" in lib.flb_last_error()
+    x.world = 9
+    assert lib.flb_decode_merge_peers(ctypes.byref(x), 0, 1, 1, 32, 128, 1, 0, None, 0, 0, None,
+                                      None, None) == _capi.FLB_ERR_INVALID_ARGUMENT
+    assert lib.flb_peer_alloc(0, ctypes.byref(ctypes.c_void_p()), None) \
+        == _capi.FLB_ERR_INVALID_ARGUMENT

@@ -215,3 +215,114 @@ def test_two_gpus_over_nccl():
     for p in procs:
         p.join(timeout=300)
         assert p.exitcode == 0
+
+
+@pytest.mark.gpu
+def test_peer_exchange_single_rank_matches_all_gather_path():
+    # World of one: the push kernel writes into this rank's own exchange buffer and the merge
+    # waits on its own counters. Same partials and merge order as the all_gather path: bitwise.
+    from flash_lab.distributed import PeerExchange
+
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    batch, heads, heads_kv, smax, d, splits = 2, 32, 8, 4096, 128, 3
+    kc = torch.randn(batch, smax, heads_kv, d, device="cuda", dtype=torch.bfloat16, generator=gen)
+    vc = torch.randn(batch, smax, heads_kv, d, device="cuda", dtype=torch.bfloat16, generator=gen)
+    lens = torch.tensor([4000, 1234], device="cuda", dtype=torch.int32)
+    shard = ShardSpec(0, smax)
+    ex = PeerExchange(batch, heads, d, splits_per_rank=splits)
+    try:
+        for step in range(3):   # parities 0, 1, 0
+            q = torch.randn(batch, heads, d, device="cuda", dtype=torch.bfloat16, generator=gen)
+            o_ref, lse_ref = decode_sharded(q, kc, vc, lens, shard, splits_per_rank=splits,
+                                            return_lse=True)
+            o, lse = decode_sharded(q, kc, vc, lens, shard, splits_per_rank=splits,
+                                    return_lse=True, exchange=ex)
+            assert torch.equal(o, o_ref) and torch.equal(lse, lse_ref), step
+        assert ex.read_status() == 0
+        assert ex.steps == 3
+    finally:
+        ex.close()
+
+
+@pytest.mark.gpu
+def test_peer_exchange_wait_times_out_with_a_status():
+    # A merge whose expected arrivals never come: the device wait gives up after its timeout,
+    # writes status 2 and returns; the GPU stays usable.
+    from flash_lab.distributed import PeerExchange
+
+    ex = PeerExchange(1, 8, 64, splits_per_rank=1, timeout_s=0.02)
+    try:
+        lib = _capi.load()
+        o = torch.zeros(1, 8, 64, device="cuda", dtype=torch.bfloat16)
+        lse = torch.zeros(1, 8, device="cuda")
+        rc = lib.flb_decode_merge_peers(ctypes.byref(ex.x), 0, 1, 1, 8, 64, 1, _capi.FLB_BF16,
+                                        o.data_ptr(), o.stride(0), o.stride(1), lse.data_ptr(),
+                                        ex.status.data_ptr(),
+                                        torch.cuda.current_stream().cuda_stream)
+        assert rc == 0
+        assert ex.read_status() == 2
+        assert not o.any()                      # nothing merged
+        q = torch.randn(1, 1, 8, 64, device="cuda", dtype=torch.bfloat16)
+        kc = torch.randn(1, 128, 8, 64, device="cuda", dtype=torch.bfloat16)
+        lens = torch.tensor([100], device="cuda", dtype=torch.int32)
+        import flash_lab
+
+        flash_lab.decode(q, kc, kc, lens)       # the context still works
+        torch.cuda.synchronize()
+    finally:
+        ex.close()
+
+
+def _peer_rank(rank, world, port, seed):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    import datetime
+
+    from flash_lab.distributed import PeerExchange
+
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    ex = None
+    try:
+        gen = torch.Generator(device="cuda").manual_seed(seed)
+        heads, heads_kv, smax, d, splits = 32, 8, 8192, 128, 2
+        kc = torch.randn(2, smax, heads_kv, d, device="cuda", dtype=torch.bfloat16, generator=gen)
+        vc = torch.randn(2, smax, heads_kv, d, device="cuda", dtype=torch.bfloat16, generator=gen)
+        lens = torch.tensor([8000, 3000], device="cuda", dtype=torch.int32)  # 2nd: one shard only
+        shard = ShardSpec.even(smax, world, rank)
+        ks = kc[:, shard.offset:shard.offset + shard.length]
+        vs = vc[:, shard.offset:shard.offset + shard.length]
+        ex = PeerExchange(2, heads, d, splits_per_rank=splits)
+        for step in range(4):
+            q = torch.randn(2, heads, d, device="cuda", dtype=torch.bfloat16, generator=gen)
+            o_ref, lse_ref = decode_sharded(q, ks, vs, lens, shard, splits_per_rank=splits,
+                                            return_lse=True)
+            o, lse = decode_sharded(q, ks, vs, lens, shard, splits_per_rank=splits,
+                                    return_lse=True, exchange=ex)
+            torch.cuda.synchronize()
+            assert torch.equal(o, o_ref) and torch.equal(lse, lse_ref), (rank, step)
+        assert ex.read_status() == 0
+        ref = oracle.decode(q.double().cpu().numpy(), kc.double().cpu().numpy(),
+                            vc.double().cpu().numpy(), lens.cpu().numpy())
+        err = np.abs(o.double().cpu().numpy() - ref).max()
+        rounding = np.abs(torch.from_numpy(ref).bfloat16().double().numpy() - ref).max()
+        assert err <= 2 * rounding, (rank, err, rounding)
+    finally:
+        if ex is not None:
+            ex.close()
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_two_gpus_over_peer_memory():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_rank, args=(r, 2, port, 7)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0
