@@ -250,7 +250,8 @@ def main() -> int:
     ap.add_argument("--no-extra", action="store_true", help="skip the secondary configurations")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--profile", default=None,
-                    choices=["prefill", "prefill_causal", "decode_mha", "decode_gqa"],
+                    choices=["prefill", "prefill_causal", "decode_mha", "decode_gqa",
+                             "decode_gqa_ragged"],
                     help="run only warmup + steps launches of one kernel (for ncu captures)")
     ap.add_argument("--batch", type=int, default=None, help="batch size of --profile")
     ap.add_argument("--e2e-llama", action="store_true",
@@ -603,8 +604,11 @@ def run_profile_case(args) -> int:
         kc = torch.randn(b, smax, hk, d, device=device, dtype=torch.bfloat16, generator=gen)
         vc = torch.randn(b, smax, hk, d, device=device, dtype=torch.bfloat16, generator=gen)
         lens = torch.full((b,), smax, device=device, dtype=torch.int32)
+        if args.profile == "decode_gqa_ragged":   # the bench's lengths, U[16384, 32768]
+            lens = torch.randint(16384, smax + 1, (b,), generator=torch.Generator().manual_seed(0))
+            lens = lens.to(device=device, dtype=torch.int32)
         fn = lambda: flash_lab.decode(qd, kc, vc, lens)  # noqa: E731
-        what = f"decode B={b} H=32 H_kv={hk} S=32768 D=128"
+        what = f"decode B={b} H=32 H_kv={hk} S=32768 D=128 lengths={lens.tolist()}"
     for _ in range(args.warmup + args.steps):
         fn()
     torch.cuda.synchronize()
