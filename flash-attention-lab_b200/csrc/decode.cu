@@ -113,6 +113,71 @@ __device__ __forceinline__ void publish_push(const DecodeArgs& a) {
   }
 }
 
+// One output element in the output dtype (round to nearest even for the 16-bit types).
+template <typename T>
+__device__ __forceinline__ void store_out(T* p, float v) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    *p = __float2bfloat16_rn(v);
+  } else if constexpr (std::is_same<T, __half>::value) {
+    *p = __float2half_rn(v);
+  } else {
+    *p = v;
+  }
+}
+
+// The end of a split CTA, shared by the 16-bit and the fp32 kernels: the consumer warps have
+// left their per-warp (m, l, O) in shared memory (wm, wl [warps][16], wo [warps][16][D]). Merges
+// the warps in a fixed order and writes either o / lse (one split) or this split's partials to
+// every destination, then publishes a push. Called by the 128 consumer threads.
+template <typename T, int D>
+__device__ __forceinline__ void finish_split(const DecodeArgs& a, const float* wm, const float* wl,
+                                             const float* wo, int heads_here, int head0, int b,
+                                             int split) {
+  const int tid = threadIdx.x;
+  for (int idx = tid; idx < heads_here * D; idx += kDecodeConsumerWarps * 32) {
+    const int row = idx / D;
+    const int d = idx - row * D;
+    float m = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kDecodeConsumerWarps; ++w) m = fmaxf(m, wm[w * kMaxHeadsPerCta + row]);
+    float num = 0.f, den = 0.f;
+#pragma unroll
+    for (int w = 0; w < kDecodeConsumerWarps; ++w) {
+      const float mw = wm[w * kMaxHeadsPerCta + row];
+      if (mw != -INFINITY) {
+        const float f = ex2(mw - m);
+        num += wo[(w * kMaxHeadsPerCta + row) * D + d] * f;
+        den += wl[w * kMaxHeadsPerCta + row] * f;
+      }
+    }
+    const int h = head0 + row;
+    if (!a.write_partials) {
+      T* o = static_cast<T*>(a.o) + static_cast<int64_t>(b) * a.o_batch_stride +
+             static_cast<int64_t>(h) * a.o_head_stride;
+      store_out<T>(o + d, den > 0.f ? num / den : 0.f);
+      if (d == 0) {
+        a.lse[static_cast<int64_t>(b) * a.heads + h] =
+            den > 0.f ? m * 0.69314718055994530942f + logf(den) : -INFINITY;
+      }
+    } else {
+      const int64_t slot =
+          (static_cast<int64_t>(b) * a.heads + h) * a.splits_total + a.split_offset + split;
+      for (int dst = 0; dst < a.n_dest; ++dst) {
+        a.partial_o[dst][slot * D + d] = num;
+        if (d == 0) {
+          a.partial_ml[dst][2 * slot] = m;
+          a.partial_ml[dst][2 * slot + 1] = den;
+        }
+      }
+    }
+  }
+  if (a.write_partials && a.arrive[0] != nullptr) {
+    asm volatile("bar.sync 1, %0;" ::"n"(kDecodeConsumerWarps * 32) : "memory");
+    if (tid == 0) publish_push(a);
+  }
+}
+
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kDecodeThreads)
     decode_split_kernel(const __grid_constant__ DecodeArgs a,
@@ -361,55 +426,252 @@ __global__ void __launch_bounds__(kDecodeThreads)
   }
   asm volatile("bar.sync 1, %0;" ::"n"(kDecodeConsumerWarps * 32) : "memory");
 
-  const int tid = threadIdx.x;
-  for (int idx = tid; idx < heads_here * D; idx += kDecodeConsumerWarps * 32) {
-    const int row = idx / D;
-    const int d = idx - row * D;
-    float m = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kDecodeConsumerWarps; ++w) m = fmaxf(m, wm[w * kMaxHeadsPerCta + row]);
-    float num = 0.f, den = 0.f;
-#pragma unroll
-    for (int w = 0; w < kDecodeConsumerWarps; ++w) {
-      const float mw = wm[w * kMaxHeadsPerCta + row];
-      if (mw != -INFINITY) {
-        const float f = ex2(mw - m);
-        num += wo[(w * kMaxHeadsPerCta + row) * D + d] * f;
-        den += wl[w * kMaxHeadsPerCta + row] * f;
+  finish_split<T, D>(a, wm, wl, wo, heads_here, head0, b, split);
+}
+
+// ---------------------------------------------------------------------------------------------
+// fp32 caches (the reference's fp32 decode): the same CTA layout and TMA producer, with fp32
+// tiles of 32 keys and the dot products on the FMA pipe (fp32 end to end, no tensor cores).
+// Each half-warp takes one key at a time: lane l owns dims {64 i + 4 (l % 16) .. + 3}, so a
+// quarter-warp reads 128 contiguous bytes of a row; a dot product is reduced over the half-warp
+// with four shuffles. kHeads (1, 2, 4 or 8) query heads of the GQA group share each K/V read.
+// ---------------------------------------------------------------------------------------------
+constexpr int kF32BK = 32;            // keys per fp32 tile
+constexpr int kF32MaxHeads = 8;       // query heads per fp32 CTA
+
+template <int D>
+struct DecodeF32Cfg {
+  static constexpr int kTileBytes = kF32BK * D * 4;    // one K or V tile: 16 KB at D = 128
+  static constexpr int kStages = D == 128 ? 3 : 6;
+  static constexpr int kStageBytes = 2 * kTileBytes;
+  static constexpr int kMergeBytes = kDecodeConsumerWarps * kMaxHeadsPerCta * (D + 2) * 4;
+  static constexpr int kRingBytes = kStages * kStageBytes;
+  static constexpr int kDataBytes = kRingBytes > kMergeBytes ? kRingBytes : kMergeBytes;
+  static constexpr int kSmemBytes = kDataBytes + 1024 + 256;
+};
+
+template <int D, int kHeads>
+__global__ void __launch_bounds__(kDecodeThreads, 2)
+    decode_split_f32_kernel(const __grid_constant__ DecodeArgs a,
+                            const __grid_constant__ CUtensorMap tmk,
+                            const __grid_constant__ CUtensorMap tmv) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  using Cfg = DecodeF32Cfg<D>;
+  constexpr int kStages = Cfg::kStages;
+  constexpr int kDL = D / 16;       // dims per lane
+  constexpr int kV4 = kDL / 4;      // float4 loads per row per lane
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + Cfg::kDataBytes);
+  uint64_t* empty_bar = full_bar + kStages;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(empty_bar + kStages);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const int split = blockIdx.x;
+  const int chunk = blockIdx.y % a.head_chunks;
+  const int bk = blockIdx.y / a.head_chunks;
+  const int hkv = bk % a.heads_kv;
+  const int b = bk / a.heads_kv;
+  const int head0 = hkv * a.group + chunk * kF32MaxHeads;
+  const int heads_here = min(kF32MaxHeads, a.group - chunk * kF32MaxHeads);
+
+  int len = a.seq_lens[b];
+  len = min(max(len, 0), a.max_seqlen);
+  const int lo = max(a.key_begin, 0);
+  const int hi = min(a.key_end, len);
+  const int n = hi - lo;
+  int k0 = 0, k1 = 0;
+  if (n > 0) {
+    const int per = (n + a.num_splits - 1) / a.num_splits;
+    const int per_split = (per + kDecodeBK - 1) / kDecodeBK * kDecodeBK;
+    k0 = lo + split * per_split;
+    k1 = min(hi, k0 + per_split);
+  }
+  const int ntiles = k1 > k0 ? (k1 - k0 + kF32BK - 1) / kF32BK : 0;
+
+  if (threadIdx.x == 0) {
+    *abort_flag = 0;
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], kDecodeConsumerWarps);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const WaitGuard guard{abort_flag, a.status};
+
+  if (warp == kDecodeConsumerWarps) {
+    // ---------------- producer warp: one [32 keys x D] fp32 box per K or V tile ----------------
+    if (lane == 0 && ntiles > 0) {
+      tma_prefetch_desc(&tmk);
+      tma_prefetch_desc(&tmv);
+      for (int t = 0; t < ntiles; ++t) {
+        const int s = t % kStages;
+        if (t >= kStages) {
+          if (!mbar_wait(&empty_bar[s], ((t / kStages) - 1) & 1, guard)) break;
+        }
+        uint8_t* kdst = smem + s * Cfg::kStageBytes;
+        mbar_arrive_expect_tx(&full_bar[s], Cfg::kStageBytes);
+        const int key = k0 + t * kF32BK;
+        tma_load_4d(kdst, &tmk, &full_bar[s], 0, tma_c(a.kc, 1, key, hkv, b),
+                    tma_c(a.kc, 2, key, hkv, b), tma_c(a.kc, 3, key, hkv, b));
+        tma_load_4d(kdst + Cfg::kTileBytes, &tmv, &full_bar[s], 0, tma_c(a.vc, 1, key, hkv, b),
+                    tma_c(a.vc, 2, key, hkv, b), tma_c(a.vc, 3, key, hkv, b));
+      }
+      const int first_unwaited = ntiles > kStages ? ntiles - kStages : 0;
+      for (int t = first_unwaited; t < ntiles; ++t) {
+        if (!mbar_wait(&full_bar[t % kStages], (t / kStages) & 1, guard)) break;
       }
     }
-    const int h = head0 + row;
-    if (!a.write_partials) {
-      T* o = static_cast<T*>(a.o) + static_cast<int64_t>(b) * a.o_batch_stride +
-             static_cast<int64_t>(h) * a.o_head_stride;
-      const float val = den > 0.f ? num / den : 0.f;
-      if constexpr (sizeof(T) == 2) {
-        if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-          o[d] = __float2bfloat16_rn(val);
-        } else {
-          o[d] = __float2half_rn(val);
-        }
-      }
-      if (d == 0) {
-        a.lse[static_cast<int64_t>(b) * a.heads + h] =
-            den > 0.f ? m * 0.69314718055994530942f + logf(den) : -INFINITY;
-      }
-    } else {
-      const int64_t slot =
-          (static_cast<int64_t>(b) * a.heads + h) * a.splits_total + a.split_offset + split;
-      for (int dst = 0; dst < a.n_dest; ++dst) {
-        a.partial_o[dst][slot * D + d] = num;
-        if (d == 0) {
-          a.partial_ml[dst][2 * slot] = m;
-          a.partial_ml[dst][2 * slot + 1] = den;
-        }
+    return;
+  }
+
+  // ---------------- consumer warps: 8 keys of every tile, 4 per half-warp ----------------
+  const int half = lane >> 4;
+  const int hl = lane & 15;
+  float q[kHeads][kDL];
+  {
+    const float* qb = static_cast<const float*>(a.q) + static_cast<int64_t>(b) * a.q_batch_stride;
+#pragma unroll
+    for (int h = 0; h < kHeads; ++h) {
+      const float* qh = qb + static_cast<int64_t>(head0 + h) * a.q_head_stride;
+#pragma unroll
+      for (int i = 0; i < kV4; ++i) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (h < heads_here) v = *reinterpret_cast<const float4*>(qh + i * 64 + hl * 4);
+        q[h][4 * i + 0] = v.x * a.scale_log2;
+        q[h][4 * i + 1] = v.y * a.scale_log2;
+        q[h][4 * i + 2] = v.z * a.scale_log2;
+        q[h][4 * i + 3] = v.w * a.scale_log2;
       }
     }
   }
-  if (a.write_partials && a.arrive[0] != nullptr) {
-    asm volatile("bar.sync 1, %0;" ::"n"(kDecodeConsumerWarps * 32) : "memory");
-    if (tid == 0) publish_push(a);
+  float o[kHeads][kDL];
+  float m_run[kHeads], l_run[kHeads];
+#pragma unroll
+  for (int h = 0; h < kHeads; ++h) {
+    m_run[h] = -INFINITY;
+    l_run[h] = 0.f;
+#pragma unroll
+    for (int i = 0; i < kDL; ++i) o[h][i] = 0.f;
   }
+
+  bool ok = true;
+  for (int t = 0; t < ntiles; ++t) {
+    const int s = t % kStages;
+    if (!mbar_wait(&full_bar[s], (t / kStages) & 1, guard)) {
+      ok = false;
+      break;
+    }
+    const float* kt = reinterpret_cast<const float*>(smem + s * Cfg::kStageBytes);
+    const float* vt = kt + kF32BK * D;
+    const int row0 = warp * 8 + half * 4;              // this half's first key in the tile
+    const int valid = k1 - (k0 + t * kF32BK + row0);   // its keys before the split's end
+
+    float sc[4][kHeads];
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      float kv[kDL];
+      const float* krow = kt + (row0 + kk) * D + hl * 4;
+#pragma unroll
+      for (int i = 0; i < kV4; ++i) {
+        const float4 v = *reinterpret_cast<const float4*>(krow + i * 64);
+        kv[4 * i + 0] = v.x;
+        kv[4 * i + 1] = v.y;
+        kv[4 * i + 2] = v.z;
+        kv[4 * i + 3] = v.w;
+      }
+#pragma unroll
+      for (int h = 0; h < kHeads; ++h) {
+        float dot = 0.f;
+#pragma unroll
+        for (int i = 0; i < kDL; ++i) dot = fmaf(q[h][i], kv[i], dot);
+        dot += __shfl_xor_sync(0xffffffffu, dot, 8);
+        dot += __shfl_xor_sync(0xffffffffu, dot, 4);
+        dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+        dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+        sc[kk][h] = kk < valid ? dot : -INFINITY;
+      }
+    }
+    // Online softmax over the warp's 8 keys (exp2 domain; q carries the scale).
+    float ref[kHeads];
+#pragma unroll
+    for (int h = 0; h < kHeads; ++h) {
+      float mt = fmaxf(fmaxf(sc[0][h], sc[1][h]), fmaxf(sc[2][h], sc[3][h]));
+      mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+      const float m_new = fmaxf(m_run[h], mt);
+      ref[h] = m_new == -INFINITY ? 0.f : m_new;
+      const float resc = ex2(m_run[h] - ref[h]);
+      m_run[h] = m_new;
+      l_run[h] *= resc;
+#pragma unroll
+      for (int i = 0; i < kDL; ++i) o[h][i] *= resc;
+    }
+    // O += P V over this half's valid keys (V rows of hidden keys are never read: 0 * NaN).
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      if (kk < valid) {
+        float vv[kDL];
+        const float* vrow = vt + (row0 + kk) * D + hl * 4;
+#pragma unroll
+        for (int i = 0; i < kV4; ++i) {
+          const float4 v = *reinterpret_cast<const float4*>(vrow + i * 64);
+          vv[4 * i + 0] = v.x;
+          vv[4 * i + 1] = v.y;
+          vv[4 * i + 2] = v.z;
+          vv[4 * i + 3] = v.w;
+        }
+#pragma unroll
+        for (int h = 0; h < kHeads; ++h) {
+          const float p = ex2(sc[kk][h] - ref[h]);
+          l_run[h] += p;
+#pragma unroll
+          for (int i = 0; i < kDL; ++i) o[h][i] = fmaf(p, vv[i], o[h][i]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[s]);
+  }
+
+  // The two halves saw different keys with the same reference point: add them up.
+#pragma unroll
+  for (int h = 0; h < kHeads; ++h) {
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 16);
+#pragma unroll
+    for (int i = 0; i < kDL; ++i) o[h][i] += __shfl_xor_sync(0xffffffffu, o[h][i], 16);
+  }
+
+  asm volatile("bar.sync 1, %0;" ::"n"(kDecodeConsumerWarps * 32) : "memory");
+  if (!ok || *abort_flag) {
+    if (a.write_partials && a.arrive[0] != nullptr && threadIdx.x == 0) publish_push(a);
+    return;
+  }
+  float* wm = reinterpret_cast<float*>(smem);                         // [warps][16]
+  float* wl = wm + kDecodeConsumerWarps * kMaxHeadsPerCta;            // [warps][16]
+  float* wo = wl + kDecodeConsumerWarps * kMaxHeadsPerCta;            // [warps][16][D]
+  if (half == 0) {
+#pragma unroll
+    for (int h = 0; h < kHeads; ++h) {
+      if (hl == 0) {
+        wm[warp * kMaxHeadsPerCta + h] = m_run[h];
+        wl[warp * kMaxHeadsPerCta + h] = l_run[h];
+      }
+      float* row = wo + (warp * kMaxHeadsPerCta + h) * D + hl * 4;
+#pragma unroll
+      for (int i = 0; i < kV4; ++i) {
+        *reinterpret_cast<float4*>(row + i * 64) =
+            make_float4(o[h][4 * i], o[h][4 * i + 1], o[h][4 * i + 2], o[h][4 * i + 3]);
+      }
+    }
+  }
+  asm volatile("bar.sync 1, %0;" ::"n"(kDecodeConsumerWarps * 32) : "memory");
+
+  finish_split<float, D>(a, wm, wl, wo, heads_here, head0, b, split);
 }
 
 // Arrivals a merge waits for: counters[src] >= expected for every source rank (null = none).
@@ -472,13 +734,8 @@ __global__ void decode_merge_kernel(const float* __restrict__ partial_o,
         den += load(partial_ml + 2 * (base + s) + 1) * f;
       }
     }
-    const float val = den > 0.f ? num / den : 0.f;
     T* out = o + static_cast<int64_t>(b) * o_batch_stride + static_cast<int64_t>(h) * o_head_stride;
-    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-      out[d] = __float2bfloat16_rn(val);
-    } else {
-      out[d] = __float2half_rn(val);
-    }
+    store_out<T>(out + d, den > 0.f ? num / den : 0.f);
     if (d == 0) lse[bh] = den > 0.f ? m * 0.69314718055994530942f + logf(den) : -INFINITY;
   }
 }
@@ -536,35 +793,42 @@ int validate(const flb_decode_params* p) {
     return fail(FLB_ERR_INVALID_ARGUMENT,
                 "the number of query heads (%d) must be a multiple of KV heads (%d)", p->heads,
                 p->heads_kv);
-  if (p->dtype != FLB_BF16 && p->dtype != FLB_FP16)
-    return fail(FLB_ERR_UNSUPPORTED, "decode takes bf16 or fp16 (dtype code %d)", p->dtype);
+  if (p->dtype != FLB_BF16 && p->dtype != FLB_FP16 && p->dtype != FLB_FP32)
+    return fail(FLB_ERR_UNSUPPORTED, "decode takes bf16, fp16 or fp32 (dtype code %d)",
+                p->dtype);
   if (p->head_dim != 64 && p->head_dim != 128)
     return fail(FLB_ERR_UNSUPPORTED, "unsupported head_dim %d (64 or 128)", p->head_dim);
   if (!(p->softmax_scale > 0.f))
     return fail(FLB_ERR_INVALID_ARGUMENT, "softmax_scale must be positive");
   if (p->num_splits < 0 || p->num_splits > kMaxSplits)
     return fail(FLB_ERR_INVALID_ARGUMENT, "num_splits must be in [0, %d]", kMaxSplits);
+  const int64_t esize = p->dtype == FLB_FP32 ? 4 : 2;
   if (reinterpret_cast<uintptr_t>(p->q) % 16 != 0 ||
-      (p->batch > 1 && (p->q_batch_stride * 2) % 16 != 0) ||
-      (p->heads > 1 && (p->q_head_stride * 2) % 16 != 0))
+      (p->batch > 1 && (p->q_batch_stride * esize) % 16 != 0) ||
+      (p->heads > 1 && (p->q_head_stride * esize) % 16 != 0))
     return fail(FLB_ERR_MISALIGNED, "q must have 16-byte aligned rows");
   return FLB_OK;
 }
 
 int build_maps(const flb_decode_params* p, CUtensorMap* tmk, CUtensorMap* tmv, TmaCoords* kc,
                TmaCoords* vc) {
+  const int esize = p->dtype == FLB_FP32 ? 4 : 2;
   View4 kv{p->k_cache,
            {p->batch, p->max_seqlen, p->heads_kv, p->head_dim},
            {p->k_batch_stride, p->k_seq_stride, p->k_head_stride, 1},
-           2};
+           esize};
   View4 vv{p->v_cache,
            {p->batch, p->max_seqlen, p->heads_kv, p->head_dim},
            {p->v_batch_stride, p->v_seq_stride, p->v_head_stride, 1},
-           2};
+           esize};
   if (!rows_16b_aligned(kv))
     return fail(FLB_ERR_MISALIGNED, "k_cache must have 16-byte aligned rows (data pointer and strides)");
   if (!rows_16b_aligned(vv))
     return fail(FLB_ERR_MISALIGNED, "v_cache must have 16-byte aligned rows (data pointer and strides)");
+  if (p->dtype == FLB_FP32) {   // [32 keys x D] fp32 boxes, unswizzled
+    if (int st = encode_rows_map(tmk, kc, kv, kF32BK, p->head_dim, FLB_FP32, false)) return st;
+    return encode_rows_map(tmv, vc, vv, kF32BK, p->head_dim, FLB_FP32, false);
+  }
   if (int st = encode_rows_x64_map(tmk, kc, kv, kDecodeBK, p->dtype)) return st;
   return encode_rows_x64_map(tmv, vc, vv, kDecodeBK, p->dtype);
 }
@@ -584,7 +848,8 @@ DecodeArgs make_args(const flb_decode_params* p) {
   a.heads = p->heads;
   a.heads_kv = p->heads_kv;
   a.group = p->heads / p->heads_kv;
-  a.head_chunks = (a.group + kMaxHeadsPerCta - 1) / kMaxHeadsPerCta;
+  const int heads_per_cta = p->dtype == FLB_FP32 ? kF32MaxHeads : kMaxHeadsPerCta;
+  a.head_chunks = (a.group + heads_per_cta - 1) / heads_per_cta;
   a.max_seqlen = p->max_seqlen;
   a.scale_log2 = static_cast<float>(static_cast<double>(p->softmax_scale) * 1.4426950408889634);
   a.key_begin = 0;
@@ -592,14 +857,67 @@ DecodeArgs make_args(const flb_decode_params* p) {
   return a;
 }
 
-template <typename F>
-int dispatch(int dtype, int head_dim, F&& f) {
-  if (dtype == FLB_BF16) {
-    if (head_dim == 128) return f(__nv_bfloat16{}, std::integral_constant<int, 128>{});
-    return f(__nv_bfloat16{}, std::integral_constant<int, 64>{});
+template <int D, int kHeads>
+int launch_split_f32(const DecodeArgs& args, const CUtensorMap& tmk, const CUtensorMap& tmv,
+                     int grid_x, int grid_y, cudaStream_t stream) {
+  using Cfg = DecodeF32Cfg<D>;
+  static thread_local int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    if (int st = check_cuda(cudaFuncSetAttribute(decode_split_f32_kernel<D, kHeads>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 Cfg::kSmemBytes),
+                            "cudaFuncSetAttribute(decode f32)"))
+      return st;
+    configured_device = dev;
   }
-  if (head_dim == 128) return f(__half{}, std::integral_constant<int, 128>{});
-  return f(__half{}, std::integral_constant<int, 64>{});
+  decode_split_f32_kernel<D, kHeads>
+      <<<dim3(grid_x, grid_y), kDecodeThreads, Cfg::kSmemBytes, stream>>>(args, tmk, tmv);
+  return check_cuda(cudaGetLastError(), "decode_split_f32_kernel launch");
+}
+
+template <int D>
+int launch_split_f32_heads(const DecodeArgs& a, const CUtensorMap& tmk, const CUtensorMap& tmv,
+                           int grid_x, int grid_y, cudaStream_t stream) {
+  // Query heads a CTA holds in registers: the group (a power of two at least as large), at most 8.
+  if (a.group >= 5) return launch_split_f32<D, 8>(a, tmk, tmv, grid_x, grid_y, stream);
+  if (a.group >= 3) return launch_split_f32<D, 4>(a, tmk, tmv, grid_x, grid_y, stream);
+  if (a.group == 2) return launch_split_f32<D, 2>(a, tmk, tmv, grid_x, grid_y, stream);
+  return launch_split_f32<D, 1>(a, tmk, tmv, grid_x, grid_y, stream);
+}
+
+// The split kernel for any supported (dtype, head_dim).
+int launch_split_any(int dtype, int head_dim, const DecodeArgs& a, const CUtensorMap& tmk,
+                     const CUtensorMap& tmv, int grid_x, int grid_y, cudaStream_t stream) {
+  if (dtype == FLB_FP32) {
+    if (head_dim == 128) return launch_split_f32_heads<128>(a, tmk, tmv, grid_x, grid_y, stream);
+    return launch_split_f32_heads<64>(a, tmk, tmv, grid_x, grid_y, stream);
+  }
+  if (dtype == FLB_BF16) {
+    if (head_dim == 128)
+      return launch_split<__nv_bfloat16, 128>(a, tmk, tmv, grid_x, grid_y, stream);
+    return launch_split<__nv_bfloat16, 64>(a, tmk, tmv, grid_x, grid_y, stream);
+  }
+  if (head_dim == 128) return launch_split<__half, 128>(a, tmk, tmv, grid_x, grid_y, stream);
+  return launch_split<__half, 64>(a, tmk, tmv, grid_x, grid_y, stream);
+}
+
+// The merge kernel for any output dtype.
+template <bool kPeers = false>
+int launch_merge_any(int dtype, const float* po, const float* pml, int batch, int heads,
+                     int head_dim, int splits, void* o, int64_t obs, int64_t ohs, float* lse,
+                     cudaStream_t stream, PeerWait wait = PeerWait{}) {
+  if (dtype == FLB_BF16)
+    return launch_merge<__nv_bfloat16, kPeers>(po, pml, batch, heads, head_dim, splits, o, obs,
+                                               ohs, lse, stream, wait);
+  if (dtype == FLB_FP16)
+    return launch_merge<__half, kPeers>(po, pml, batch, heads, head_dim, splits, o, obs, ohs, lse,
+                                        stream, wait);
+  if (dtype == FLB_FP32)
+    return launch_merge<float, kPeers>(po, pml, batch, heads, head_dim, splits, o, obs, ohs, lse,
+                                       stream, wait);
+  return fail(FLB_ERR_UNSUPPORTED, "merge takes bf16, fp16 or fp32 (dtype code %d)", dtype);
 }
 
 // Split count from shapes only (so a captured CUDA graph stays valid for any lengths). Measured
@@ -664,9 +982,7 @@ extern "C" int flb_decode_fwd(const flb_decode_params* p, flb_stream_t stream_) 
   a.splits_total = splits;
   if (splits == 1) {
     a.write_partials = 0;
-    return dispatch(p->dtype, p->head_dim, [&](auto tag, auto dim) {
-      return launch_split<decltype(tag), decltype(dim)::value>(a, tmk, tmv, 1, grid_y, stream);
-    });
+    return launch_split_any(p->dtype, p->head_dim, a, tmk, tmv, 1, grid_y, stream);
   }
   const size_t need = flb_decode_workspace_bytes(p->batch, p->heads, p->head_dim, splits);
   if (p->workspace == nullptr || p->workspace_bytes < need)
@@ -680,13 +996,11 @@ extern "C" int flb_decode_fwd(const flb_decode_params* p, flb_stream_t stream_) 
   a.partial_ml[0] = reinterpret_cast<float*>(
       static_cast<char*>(p->workspace) + (slots * p->head_dim * sizeof(float) + 255) / 256 * 256);
   a.write_partials = 1;
-  return dispatch(p->dtype, p->head_dim, [&](auto tag, auto dim) {
-    using T = decltype(tag);
-    if (int st = launch_split<T, decltype(dim)::value>(a, tmk, tmv, splits, grid_y, stream))
-      return st;
-    return launch_merge<T>(a.partial_o[0], a.partial_ml[0], p->batch, p->heads, p->head_dim, splits,
-                           p->o, p->o_batch_stride, p->o_head_stride, p->lse, stream);
-  });
+  if (int st = launch_split_any(p->dtype, p->head_dim, a, tmk, tmv, splits, grid_y, stream))
+    return st;
+  return launch_merge_any(p->dtype, a.partial_o[0], a.partial_ml[0], p->batch, p->heads,
+                          p->head_dim, splits, p->o, p->o_batch_stride, p->o_head_stride, p->lse,
+                          stream);
 }
 
 extern "C" int flb_decode_partials(const flb_decode_params* p, int32_t key_begin,
@@ -725,10 +1039,7 @@ extern "C" int flb_decode_partials(const flb_decode_params* p, int32_t key_begin
   if (grid_y > 65535)
     return fail(FLB_ERR_UNSUPPORTED, "batch * heads_kv * head chunks = %d exceeds 65535", grid_y);
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
-  return dispatch(q.dtype, q.head_dim, [&](auto tag, auto dim) {
-    return launch_split<decltype(tag), decltype(dim)::value>(a, tmk, tmv, q.num_splits, grid_y,
-                                                             stream);
-  });
+  return launch_split_any(q.dtype, q.head_dim, a, tmk, tmv, q.num_splits, grid_y, stream);
 }
 
 extern "C" int flb_decode_merge(const float* partial_o, const float* partial_ml, int32_t batch,
@@ -741,13 +1052,8 @@ extern "C" int flb_decode_merge(const float* partial_o, const float* partial_ml,
   if (batch <= 0 || heads <= 0 || num_splits <= 0 || (head_dim != 64 && head_dim != 128))
     return fail(FLB_ERR_INVALID_ARGUMENT, "bad merge shape");
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
-  if (dtype == FLB_BF16)
-    return launch_merge<__nv_bfloat16>(partial_o, partial_ml, batch, heads, head_dim, num_splits,
-                                       o, o_batch_stride, o_head_stride, lse, stream);
-  if (dtype == FLB_FP16)
-    return launch_merge<__half>(partial_o, partial_ml, batch, heads, head_dim, num_splits, o,
-                                o_batch_stride, o_head_stride, lse, stream);
-  return fail(FLB_ERR_UNSUPPORTED, "merge takes bf16 or fp16");
+  return launch_merge_any(dtype, partial_o, partial_ml, batch, heads, head_dim, num_splits, o,
+                          o_batch_stride, o_head_stride, lse, stream);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -841,10 +1147,7 @@ extern "C" int flb_decode_partials_push(const flb_decode_params* p, int32_t key_
   if (grid_y > 65535)
     return fail(FLB_ERR_UNSUPPORTED, "batch * heads_kv * head chunks = %d exceeds 65535", grid_y);
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
-  return dispatch(q.dtype, q.head_dim, [&](auto tag, auto dim) {
-    return launch_split<decltype(tag), decltype(dim)::value>(a, tmk, tmv, q.num_splits, grid_y,
-                                                             stream);
-  });
+  return launch_split_any(q.dtype, q.head_dim, a, tmk, tmv, q.num_splits, grid_y, stream);
 }
 
 extern "C" int flb_decode_merge_peers(const flb_peer_exchange* x, int32_t parity,
@@ -871,11 +1174,6 @@ extern "C" int flb_decode_merge_peers(const flb_peer_exchange* x, int32_t parity
   wait.status = status;
   const int splits = x->world * splits_per_rank;
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
-  if (dtype == FLB_BF16)
-    return launch_merge<__nv_bfloat16, true>(po, pml, batch, heads, head_dim, splits, o,
-                                             o_batch_stride, o_head_stride, lse, stream, wait);
-  if (dtype == FLB_FP16)
-    return launch_merge<__half, true>(po, pml, batch, heads, head_dim, splits, o,
-                                      o_batch_stride, o_head_stride, lse, stream, wait);
-  return fail(FLB_ERR_UNSUPPORTED, "merge takes bf16 or fp16");
+  return launch_merge_any<true>(dtype, po, pml, batch, heads, head_dim, splits, o,
+                                o_batch_stride, o_head_stride, lse, stream, wait);
 }

@@ -99,6 +99,11 @@ bool rows_16b_aligned(const View4& v) {
 
 int encode_rows_x64_map(CUtensorMap* map, TmaCoords* coords, const View4& v, int box_rows,
                         int dtype) {
+  return encode_rows_map(map, coords, v, box_rows, 64, dtype, true);
+}
+
+int encode_rows_map(CUtensorMap* map, TmaCoords* coords, const View4& v, int box_rows,
+                    int box_cols, int dtype, bool swizzle128) {
   if (!rows_16b_aligned(v)) {
     return fail(FLB_ERR_MISALIGNED,
                 "tensor must have 16-byte aligned rows (data pointer and strides)");
@@ -131,7 +136,7 @@ int encode_rows_x64_map(CUtensorMap* map, TmaCoords* coords, const View4& v, int
   cuuint32_t box[4];
   cuuint32_t elem_strides[4] = {1, 1, 1, 1};
   dims[0] = static_cast<cuuint64_t>(v.size[3]);
-  box[0] = 64;
+  box[0] = static_cast<cuuint32_t>(box_cols);
   int64_t prev_bytes = v.size[3] * v.elem_bytes;
   int8_t pos[3] = {0, 0, 0};
   for (int j = 0; j < 3; ++j) {
@@ -153,9 +158,12 @@ int encode_rows_x64_map(CUtensorMap* map, TmaCoords* coords, const View4& v, int
   coords->pos_h = pos[2];
   coords->pad = 0;
   const CUtensorMapDataType type =
-      dtype == FLB_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+      dtype == FLB_FP32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+      : dtype == FLB_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                          : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUresult r = encode(map, type, 4, const_cast<void*>(v.base), dims, strides, box, elem_strides,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     return fail(FLB_ERR_CUDA,

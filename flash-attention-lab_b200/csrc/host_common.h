@@ -41,6 +41,12 @@ struct TmaCoords {
 int encode_rows_x64_map(CUtensorMap* map, TmaCoords* coords, const View4& v, int box_rows,
                         int dtype);
 
+// The general form: a [box_rows along S] x [box_cols along D] box, 128-byte swizzled or not
+// (box_cols * element size must be a multiple of 16 bytes; 64 columns of 16-bit elements when
+// swizzled).
+int encode_rows_map(CUtensorMap* map, TmaCoords* coords, const View4& v, int box_rows,
+                    int box_cols, int dtype, bool swizzle128);
+
 // The 16-byte row rule every kernel here relies on: base pointer and every stride of a dimension
 // longer than 1 are multiples of 16 bytes, and the head_dim stride is 1.
 bool rows_16b_aligned(const View4& v);

@@ -25,6 +25,7 @@ FLB_ERR_NO_DEVICE = 6
 
 FLB_BF16 = 0
 FLB_FP16 = 1
+FLB_FP32 = 2
 
 FLB_MAX_PEERS = 8
 

@@ -68,7 +68,9 @@ def _dtype_code(dtype: torch.dtype) -> int:
         return _capi.FLB_BF16
     if dtype == torch.float16:
         return _capi.FLB_FP16
-    raise ValueError(f"sharded decode takes bf16 or fp16, got {dtype}")
+    if dtype == torch.float32:
+        return _capi.FLB_FP32
+    raise ValueError(f"sharded decode takes bf16, fp16 or fp32, got {dtype}")
 
 
 def shard_partials(q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.Tensor,

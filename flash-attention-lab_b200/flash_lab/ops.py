@@ -38,6 +38,8 @@ else:
     EXTENSION_ERROR = ""
 
 _DTYPE_CODE = {torch.bfloat16: _capi.FLB_BF16, torch.float16: _capi.FLB_FP16}
+# The decode kernels also take fp32 caches (the reference's fp32 decode); prefill does not.
+_DECODE_DTYPE_CODE = {**_DTYPE_CODE, torch.float32: _capi.FLB_FP32}
 DEBUG = os.environ.get("FLASH_LAB_DEBUG", "0") not in ("", "0")
 
 
@@ -80,14 +82,16 @@ class DecodeImpl:
 
 
 _HALF = (torch.bfloat16, torch.float16)
+_DECODE_DTYPES = (torch.bfloat16, torch.float16, torch.float32)
 PREFILL_IMPLS: dict[str, PrefillImpl] = {
     "sm100": PrefillImpl(op="attention_sm100", dtypes=_HALF, head_dims=(64, 128)),
     "mma_pipelined": PrefillImpl(op="attention_mma_pipelined", dtypes=_HALF,
                                  head_dims=(64, 128)),
 }
 DECODE_IMPLS: dict[str, DecodeImpl] = {
-    "splitkv": DecodeImpl(op="decode_splitkv", dtypes=_HALF, head_dims=(64, 128)),
-    "decode_inplace": DecodeImpl(op="decode_inplace", dtypes=_HALF, head_dims=(64, 128)),
+    "splitkv": DecodeImpl(op="decode_splitkv", dtypes=_DECODE_DTYPES, head_dims=(64, 128)),
+    "decode_inplace": DecodeImpl(op="decode_inplace", dtypes=_DECODE_DTYPES,
+                                 head_dims=(64, 128)),
 }
 
 _PREFILL_SCHEMA = "(Tensor q, Tensor k, Tensor v, bool causal, float softmax_scale) -> (Tensor, Tensor)"
@@ -209,8 +213,8 @@ def _prefill(q, k, v, causal: bool, softmax_scale: float):
 def _decode(q, k_cache, v_cache, seq_lens, softmax_scale: float, num_splits: int,
             allow_splits: bool):
     lib = _require_library()
-    if q.dtype not in _DTYPE_CODE:
-        raise RuntimeError(f"decode takes bf16 or fp16, got {q.dtype}")
+    if q.dtype not in _DECODE_DTYPE_CODE:
+        raise RuntimeError(f"decode takes bf16, fp16 or fp32, got {q.dtype}")
     if q.dim() != 3 or k_cache.dim() != 4:
         raise RuntimeError("q must be [B, H, D], caches [B, S_max, H_kv, D]")
     if seq_lens.dtype != torch.int32 or not seq_lens.is_contiguous():
@@ -235,7 +239,7 @@ def _decode(q, k_cache, v_cache, seq_lens, softmax_scale: float, num_splits: int
         k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
         v_cache.stride(0), v_cache.stride(1), v_cache.stride(2),
         o.stride(0), o.stride(1),
-        batch, heads, heads_kv, head_dim, max_seqlen, splits, _DTYPE_CODE[q.dtype],
+        batch, heads, heads_kv, head_dim, max_seqlen, splits, _DECODE_DTYPE_CODE[q.dtype],
         float(softmax_scale),
         0 if workspace is None else workspace.data_ptr(), ws_bytes,
         _status_ptr(q.device),

@@ -48,7 +48,8 @@ typedef enum {
   FLB_ERR_NO_DEVICE = 6         /* no sm_100 device current */
 } flb_status;
 
-typedef enum { FLB_BF16 = 0, FLB_FP16 = 1 } flb_dtype;
+/* FLB_FP32 is accepted by the decode entry points only (the reference's fp32 decode). */
+typedef enum { FLB_BF16 = 0, FLB_FP16 = 1, FLB_FP32 = 2 } flb_dtype;
 
 /*
  * Prefill problem. Mirrors AttnParams (csrc/common/params.h:9-27 of the reference).
@@ -132,8 +133,8 @@ size_t flb_decode_workspace_bytes(int32_t batch, int32_t heads, int32_t head_dim
                                   int32_t num_splits);
 
 /* Split-KV decode step. Replaces the decode_splitkv / decode_inplace ops
- * (csrc/decode/decode.cu:282-340, schemas csrc/bindings.cpp:30-37). bf16 or fp16, head_dim 64
- * or 128. */
+ * (csrc/decode/decode.cu:282-340, schemas csrc/bindings.cpp:30-37). bf16, fp16 or fp32 (the
+ * reference's three decode dtypes), head_dim 64 or 128. */
 int flb_decode_fwd(const flb_decode_params* params, flb_stream_t stream);
 
 /*

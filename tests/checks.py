@@ -1,6 +1,7 @@
 """Tolerance rules for the GPU parity tests, with the numpy oracle as ground truth.
 
-Two rules are applied to every bf16/fp16 output:
+Two rules are applied to every bf16/fp16 output (fp32 decode outputs get the first, with the
+reference's fp32 floors 1e-6 / 1e-5):
   * the reference's drop-in rule (tests/test_attention_fwd.py:114-138 and
     tests/test_decode.py:256-266 of tfan2437/flash-attention-lab):
         err <= 2 * err_torch + FLOOR   (err_torch: PyTorch's own computation at the input dtype)
@@ -24,9 +25,9 @@ from torch.nn.attention import SDPBackend, sdpa_kernel
 
 import oracle
 
-FLOOR = {torch.bfloat16: 1e-3, torch.float16: 1e-3}
+FLOOR = {torch.bfloat16: 1e-3, torch.float16: 1e-3, torch.float32: 1e-6}
 GUARD = {torch.bfloat16: 2e-2, torch.float16: 1e-2}
-LSE_FLOOR = {torch.bfloat16: 1e-3, torch.float16: 1e-3}
+LSE_FLOOR = {torch.bfloat16: 1e-3, torch.float16: 1e-3, torch.float32: 1e-5}
 
 
 def host64(x: torch.Tensor) -> np.ndarray:
@@ -138,7 +139,7 @@ def check_decode(out, lse, q, k_cache, v_cache, seq_lens, scale=None, baseline_r
     err_plain = float(np.abs(host64(plain) - ref3).max())
     info = {"err": err, "err_plain": err_plain, "round": rounding_error(ref, dtype)}
     assert err <= 2 * err_plain + FLOOR[dtype], info
-    if baseline_rule:
+    if baseline_rule and dtype != torch.float32:
         assert err <= 2 * info["round"], info
     lse_err = float(np.abs(host64(lse) - ref_lse).max())
     lse_err_plain = float(np.abs(host64(plain_lse) - ref_lse).max())

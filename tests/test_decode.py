@@ -16,7 +16,7 @@ from golden_io import bf16_to_f32, load, names
 pytestmark = pytest.mark.gpu
 
 IMPLS = ["decode_inplace", "splitkv"]
-DTYPES = [torch.bfloat16, torch.float16]
+DTYPES = [torch.bfloat16, torch.float16, torch.float32]   # the reference's decode dtypes
 
 CASES = [
     # batch, heads, heads_kv, max_seqlen, head_dim, seq_lens
@@ -73,49 +73,56 @@ def test_matches_reference_goldens(name):
         assert np.abs(host64(lse) - g["lse"]).max() < 1e-3
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32],
+                         ids=lambda d: str(d).removeprefix("torch."))
 @pytest.mark.parametrize("num_splits", [1, 2, 8, 64, None])
-def test_split_counts(num_splits):
+def test_split_counts(num_splits, dtype):
     # More splits than tiles leaves some splits empty; they must not disturb the merge.
     gen = torch.Generator(device="cuda").manual_seed(1)
-    q, k_cache, v_cache, seq_lens = make_case((3, 16, 4, 2000, 128, [2000, 40, 777]),
-                                              torch.bfloat16, gen)
+    q, k_cache, v_cache, seq_lens = make_case((3, 16, 4, 2000, 128, [2000, 40, 777]), dtype,
+                                              gen)
     out, lse = flash_lab.decode(q, k_cache, v_cache, seq_lens, impl="splitkv",
                                 num_splits=num_splits, return_lse=True)
     check_decode(out, lse, q, k_cache, v_cache, seq_lens)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32],
+                         ids=lambda d: str(d).removeprefix("torch."))
 @pytest.mark.parametrize("impl", IMPLS)
-def test_strided_cache_and_rank3_query(impl):
+def test_strided_cache_and_rank3_query(impl, dtype):
     # Caches carved out of a larger allocation (every other KV head), q given as [B, H, D].
     gen = torch.Generator(device="cuda").manual_seed(2)
-    big = torch.randn(2, 600, 8, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+    big = torch.randn(2, 600, 8, 128, device="cuda", dtype=dtype, generator=gen)
     k_cache, v_cache = big[:, :, 0::2], big[:, :, 1::2]
-    q = torch.randn(2, 16, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+    q = torch.randn(2, 16, 128, device="cuda", dtype=dtype, generator=gen)
     seq_lens = torch.tensor([600, 123], device="cuda", dtype=torch.int32)
     out, lse = flash_lab.decode(q, k_cache, v_cache, seq_lens, impl=impl, return_lse=True)
     assert out.shape == q.shape
     check_decode(out, lse, q, k_cache, v_cache, seq_lens)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32],
+                         ids=lambda d: str(d).removeprefix("torch."))
 @pytest.mark.parametrize("impl", IMPLS)
-def test_head_major_static_cache_view(impl):
+def test_head_major_static_cache_view(impl, dtype):
     # The Hugging Face static cache: [B, H_kv, L, D] storage read as [B, L, H_kv, D].
     gen = torch.Generator(device="cuda").manual_seed(6)
-    kh = torch.randn(2, 4, 1000, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
-    vh = torch.randn(2, 4, 1000, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
-    q = torch.randn(2, 1, 16, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+    kh = torch.randn(2, 4, 1000, 128, device="cuda", dtype=dtype, generator=gen)
+    vh = torch.randn(2, 4, 1000, 128, device="cuda", dtype=dtype, generator=gen)
+    q = torch.randn(2, 1, 16, 128, device="cuda", dtype=dtype, generator=gen)
     seq_lens = torch.tensor([1000, 517], device="cuda", dtype=torch.int32)
     out, lse = flash_lab.decode(q, kh.transpose(1, 2), vh.transpose(1, 2), seq_lens, impl=impl,
                                 return_lse=True)
     check_decode(out, lse, q, kh.transpose(1, 2), vh.transpose(1, 2), seq_lens)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32],
+                         ids=lambda d: str(d).removeprefix("torch."))
 @pytest.mark.parametrize("impl", IMPLS)
-def test_unused_rows_are_never_read(impl):
+def test_unused_rows_are_never_read(impl, dtype):
     # NaN past each sequence's length must not reach the output (0 * NaN would).
     gen = torch.Generator(device="cuda").manual_seed(7)
-    q, k_cache, v_cache, seq_lens = make_case((3, 8, 2, 333, 128, [333, 70, 1]), torch.bfloat16,
-                                              gen)
+    q, k_cache, v_cache, seq_lens = make_case((3, 8, 2, 333, 128, [333, 70, 1]), dtype, gen)
     for b, n in enumerate(seq_lens.tolist()):
         k_cache[b, n:] = float("nan")
         v_cache[b, n:] = float("nan")
@@ -167,10 +174,10 @@ def test_rejects_unsupported(impl):
     tables = torch.zeros(1, 2, device="cuda", dtype=torch.int32)
     with pytest.raises(ValueError, match="paged"):
         flash_lab.decode(q.contiguous(), cache, cache, seq_lens, block_tables=tables, impl=impl)
-    q32 = torch.randn(1, 1, 4, 64, device="cuda")
-    c32 = torch.randn(1, 8, 4, 64, device="cuda")
+    q64 = torch.randn(1, 1, 4, 64, device="cuda", dtype=torch.float64)
+    c64 = torch.randn(1, 8, 4, 64, device="cuda", dtype=torch.float64)
     with pytest.raises(ValueError, match="dtype"):
-        flash_lab.decode(q32, c32, c32, seq_lens, impl=impl)
+        flash_lab.decode(q64, c64, c64, seq_lens, impl=impl)
 
 
 def _check_slices(out, lse, q, k_cache, v_cache, seq_lens, picks):
@@ -206,3 +213,15 @@ def test_baseline_gqa_32k_ragged():
     seq_lens = seq_lens.to("cuda", torch.int32)
     out, lse = flash_lab.decode(q, k_cache, v_cache, seq_lens, return_lse=True)
     _check_slices(out, lse, q, k_cache, v_cache, seq_lens, [(0, 0), (4, 5), (7, 7)])
+
+
+@pytest.mark.parametrize("group", [1, 2, 4, 8, 16])
+def test_fp32_gqa_groups_8k(group):
+    # fp32 caches at every register-tile size of the fp32 kernel (1, 2, 4, 8 heads per CTA; a
+    # group of 16 takes two CTAs per KV head), checked in full.
+    gen = torch.Generator(device="cuda").manual_seed(20 + group)
+    heads_kv = 32 // group if group <= 32 else 1
+    q, k_cache, v_cache, seq_lens = make_case((2, 32, heads_kv, 8192, 128, [8192, 5000]),
+                                              torch.float32, gen)
+    out, lse = flash_lab.decode(q, k_cache, v_cache, seq_lens, return_lse=True)
+    check_decode(out, lse, q, k_cache, v_cache, seq_lens)
