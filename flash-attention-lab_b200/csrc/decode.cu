@@ -56,6 +56,12 @@ struct DecodeArgs {
   float* partial_ml[kMaxDest];
   unsigned long long* arrive[kMaxDest];
   unsigned int* cta_done;
+  // Paged cache: block table [B, max_blocks] (row stride bt_stride), page_size rows per block,
+  // and box_rows, the rows of one TMA box (a box never crosses a page). Null for a contiguous
+  // cache, whose "block" is the sequence and whose box covers a whole tile.
+  const int32_t* block_tables;
+  int64_t bt_stride;
+  int page_size, max_blocks, box_rows;
   int* status;
   int64_t q_batch_stride, q_head_stride;
   int64_t o_batch_stride, o_head_stride;
@@ -87,12 +93,76 @@ __device__ __forceinline__ int tma_c(const TmaCoords& c, int slot, int s, int h,
   return c.pos_s == slot ? s : (c.pos_h == slot ? h : b);
 }
 
-__device__ __forceinline__ void load_kv_tile(uint8_t* dst, const CUtensorMap* map,
-                                             const TmaCoords& c, uint64_t* bar, int key, int hkv,
-                                             int b, int boxes) {
-  for (int box = 0; box < boxes; ++box) {
-    tma_load_4d(dst + box * (kDecodeBK * 128), map, bar, box * 64, tma_c(c, 1, key, hkv, b),
-                tma_c(c, 2, key, hkv, b), tma_c(c, 3, key, hkv, b));
+// The producer warp of both split kernels: streams ntiles tiles of kTileKeys keys (K then V) of
+// one (sequence b, KV head) starting at key k0 into the kStages ring. A tile is kColBoxes column
+// boxes (kColsPerBox columns, kColBoxBytes each in shared memory, rows of kRowBytes), each loaded
+// as kTileKeys / box_rows boxes of box_rows rows. For a paged cache each box's block comes from
+// the block table: the warp reads 32 table entries at a time (lane i holds page base + i) and
+// lane 0, which issues every copy, takes the entry it needs by shuffle. Keys past the split's end
+// are still loaded (zeros or other blocks' rows) and masked by the consumers.
+template <int kTileKeys, int kColBoxes, int kColsPerBox, int kColBoxBytes, int kRowBytes,
+          int kStages, int kTileBytes>
+__device__ __forceinline__ void produce_kv(const DecodeArgs& a, const CUtensorMap* tmk,
+                                           const CUtensorMap* tmv, uint8_t* ring,
+                                           uint64_t* full_bar, uint64_t* empty_bar, int k0,
+                                           int ntiles, int hkv, int b, const WaitGuard& guard,
+                                           int lane) {
+  constexpr int kStageBytes = 2 * kTileBytes;
+  if (ntiles <= 0) return;
+  if (lane == 0) {
+    tma_prefetch_desc(tmk);
+    tma_prefetch_desc(tmv);
+  }
+  const bool paged = a.block_tables != nullptr;
+  const int box_rows = paged ? a.box_rows : kTileKeys;
+  const int parts = kTileKeys / box_rows;
+  bool have_pages = false;
+  int page_base = 0, my_block = -1;
+  int issued = 0;
+  for (int t = 0; t < ntiles; ++t) {
+    const int s = t % kStages;
+    bool ok = true;
+    if (t >= kStages) ok = mbar_wait(&empty_bar[s], ((t / kStages) - 1) & 1, guard);
+    if (!__all_sync(0xffffffffu, ok)) break;
+    uint8_t* kdst = ring + s * kStageBytes;
+    uint8_t* vdst = kdst + kTileBytes;
+    if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
+    for (int j = 0; j < parts; ++j) {
+      const int key = k0 + t * kTileKeys + j * box_rows;
+      int blk = b, row = key;
+      if (paged) {
+        const int page = key / a.page_size;
+        if (!have_pages || page >= page_base + 32) {   // pages only increase along the split
+          have_pages = true;
+          page_base = page;
+          const int p = page_base + lane;
+          my_block = p < a.max_blocks
+                         ? __ldg(a.block_tables + static_cast<int64_t>(b) * a.bt_stride + p)
+                         : -1;
+        }
+        blk = __shfl_sync(0xffffffffu, my_block, page - page_base);
+        row = key - page * a.page_size;
+      }
+      if (lane == 0) {
+#pragma unroll
+        for (int cb = 0; cb < kColBoxes; ++cb) {
+          const int off = cb * kColBoxBytes + j * box_rows * kRowBytes;
+          tma_load_4d(kdst + off, tmk, &full_bar[s], cb * kColsPerBox,
+                      tma_c(a.kc, 1, row, hkv, blk), tma_c(a.kc, 2, row, hkv, blk),
+                      tma_c(a.kc, 3, row, hkv, blk));
+          tma_load_4d(vdst + off, tmv, &full_bar[s], cb * kColsPerBox,
+                      tma_c(a.vc, 1, row, hkv, blk), tma_c(a.vc, 2, row, hkv, blk),
+                      tma_c(a.vc, 3, row, hkv, blk));
+        }
+      }
+    }
+    issued = t + 1;
+  }
+  // Do not leave the CTA while copies are still landing in shared memory.
+  if (lane == 0) {
+    for (int t = issued > kStages ? issued - kStages : 0; t < issued; ++t) {
+      if (!mbar_wait(&full_bar[t % kStages], (t / kStages) & 1, guard)) break;
+    }
   }
 }
 
@@ -239,27 +309,8 @@ __global__ void __launch_bounds__(kDecodeThreads)
 
   if (warp == kDecodeConsumerWarps) {
     // ---------------- producer warp ----------------
-    if (lane == 0 && ntiles > 0) {
-      tma_prefetch_desc(&tmk);
-      tma_prefetch_desc(&tmv);
-      for (int t = 0; t < ntiles; ++t) {
-        const int s = t % kStages;
-        if (t >= kStages) {
-          if (!mbar_wait(&empty_bar[s], ((t / kStages) - 1) & 1, guard)) break;
-        }
-        uint8_t* kdst = smem + s * Cfg::kStageBytes;
-        uint8_t* vdst = kdst + Cfg::kTileBytes;
-        mbar_arrive_expect_tx(&full_bar[s], Cfg::kStageBytes);
-        const int key = k0 + t * kDecodeBK;
-        load_kv_tile(kdst, &tmk, a.kc, &full_bar[s], key, hkv, b, Cfg::kBoxes);
-        load_kv_tile(vdst, &tmv, a.vc, &full_bar[s], key, hkv, b, Cfg::kBoxes);
-      }
-      // Do not leave the CTA while copies are still landing in shared memory.
-      const int first_unwaited = ntiles > kStages ? ntiles - kStages : 0;
-      for (int t = first_unwaited; t < ntiles; ++t) {
-        if (!mbar_wait(&full_bar[t % kStages], (t / kStages) & 1, guard)) break;
-      }
-    }
+    produce_kv<kDecodeBK, Cfg::kBoxes, 64, Cfg::kBoxBytes, 128, kStages, Cfg::kTileBytes>(
+        a, &tmk, &tmv, smem, full_bar, empty_bar, k0, ntiles, hkv, b, guard, lane);
     return;
   }
 
@@ -505,28 +556,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
   const WaitGuard guard{abort_flag, a.status};
 
   if (warp == kDecodeConsumerWarps) {
-    // ---------------- producer warp: one [32 keys x D] fp32 box per K or V tile ----------------
-    if (lane == 0 && ntiles > 0) {
-      tma_prefetch_desc(&tmk);
-      tma_prefetch_desc(&tmv);
-      for (int t = 0; t < ntiles; ++t) {
-        const int s = t % kStages;
-        if (t >= kStages) {
-          if (!mbar_wait(&empty_bar[s], ((t / kStages) - 1) & 1, guard)) break;
-        }
-        uint8_t* kdst = smem + s * Cfg::kStageBytes;
-        mbar_arrive_expect_tx(&full_bar[s], Cfg::kStageBytes);
-        const int key = k0 + t * kF32BK;
-        tma_load_4d(kdst, &tmk, &full_bar[s], 0, tma_c(a.kc, 1, key, hkv, b),
-                    tma_c(a.kc, 2, key, hkv, b), tma_c(a.kc, 3, key, hkv, b));
-        tma_load_4d(kdst + Cfg::kTileBytes, &tmv, &full_bar[s], 0, tma_c(a.vc, 1, key, hkv, b),
-                    tma_c(a.vc, 2, key, hkv, b), tma_c(a.vc, 3, key, hkv, b));
-      }
-      const int first_unwaited = ntiles > kStages ? ntiles - kStages : 0;
-      for (int t = first_unwaited; t < ntiles; ++t) {
-        if (!mbar_wait(&full_bar[t % kStages], (t / kStages) & 1, guard)) break;
-      }
-    }
+    // ---------------- producer warp: [32 keys x D] fp32 tiles ----------------
+    produce_kv<kF32BK, 1, D, Cfg::kTileBytes, D * 4, kStages, Cfg::kTileBytes>(
+        a, &tmk, &tmv, smem, full_bar, empty_bar, k0, ntiles, hkv, b, guard, lane);
     return;
   }
 
@@ -802,6 +834,23 @@ int validate(const flb_decode_params* p) {
     return fail(FLB_ERR_INVALID_ARGUMENT, "softmax_scale must be positive");
   if (p->num_splits < 0 || p->num_splits > kMaxSplits)
     return fail(FLB_ERR_INVALID_ARGUMENT, "num_splits must be in [0, %d]", kMaxSplits);
+  if (p->block_tables != nullptr) {
+    const int ps = p->page_size;
+    // A 128-byte-swizzled box must start on a 1024-byte (8-row) boundary, and a box never
+    // crosses a page: pages of 8, 16 or 32 rows, or whole multiples of the 64-key tile.
+    if (ps <= 0 || !(ps == 8 || ps == 16 || ps == 32 || ps % 64 == 0))
+      return fail(FLB_ERR_UNSUPPORTED,
+                  "paged cache: page_size %d must be 8, 16, 32 or a multiple of 64", ps);
+    if (p->num_blocks <= 0)
+      return fail(FLB_ERR_INVALID_ARGUMENT, "paged cache: num_blocks must be positive");
+    if (p->max_seqlen % ps != 0)
+      return fail(FLB_ERR_INVALID_ARGUMENT,
+                  "paged cache: max_seqlen %d must be max_blocks * page_size (page_size %d)",
+                  p->max_seqlen, ps);
+    if (p->batch > 1 && p->block_table_stride < p->max_seqlen / ps)
+      return fail(FLB_ERR_INVALID_ARGUMENT, "paged cache: block_table_stride %lld < max_blocks %d",
+                  static_cast<long long>(p->block_table_stride), p->max_seqlen / ps);
+  }
   const int64_t esize = p->dtype == FLB_FP32 ? 4 : 2;
   if (reinterpret_cast<uintptr_t>(p->q) % 16 != 0 ||
       (p->batch > 1 && (p->q_batch_stride * esize) % 16 != 0) ||
@@ -810,27 +859,41 @@ int validate(const flb_decode_params* p) {
   return FLB_OK;
 }
 
+// Keys per tile of the kernel that runs p, and rows per TMA box (a box never crosses a page).
+int tile_keys_for(const flb_decode_params* p) { return p->dtype == FLB_FP32 ? kF32BK : kDecodeBK; }
+
+int box_rows_for(const flb_decode_params* p) {
+  const int tile = tile_keys_for(p);
+  return p->block_tables != nullptr ? std::min(tile, p->page_size) : tile;
+}
+
 int build_maps(const flb_decode_params* p, CUtensorMap* tmk, CUtensorMap* tmv, TmaCoords* kc,
                TmaCoords* vc) {
   const int esize = p->dtype == FLB_FP32 ? 4 : 2;
+  // A paged cache is the same 4-D view with blocks in place of sequences and pages in place of
+  // the sequence axis; its boxes are at most one page tall.
+  const bool paged = p->block_tables != nullptr;
+  const int64_t outer = paged ? p->num_blocks : p->batch;
+  const int64_t rows = paged ? p->page_size : p->max_seqlen;
   View4 kv{p->k_cache,
-           {p->batch, p->max_seqlen, p->heads_kv, p->head_dim},
+           {outer, rows, p->heads_kv, p->head_dim},
            {p->k_batch_stride, p->k_seq_stride, p->k_head_stride, 1},
            esize};
   View4 vv{p->v_cache,
-           {p->batch, p->max_seqlen, p->heads_kv, p->head_dim},
+           {outer, rows, p->heads_kv, p->head_dim},
            {p->v_batch_stride, p->v_seq_stride, p->v_head_stride, 1},
            esize};
   if (!rows_16b_aligned(kv))
     return fail(FLB_ERR_MISALIGNED, "k_cache must have 16-byte aligned rows (data pointer and strides)");
   if (!rows_16b_aligned(vv))
     return fail(FLB_ERR_MISALIGNED, "v_cache must have 16-byte aligned rows (data pointer and strides)");
-  if (p->dtype == FLB_FP32) {   // [32 keys x D] fp32 boxes, unswizzled
-    if (int st = encode_rows_map(tmk, kc, kv, kF32BK, p->head_dim, FLB_FP32, false)) return st;
-    return encode_rows_map(tmv, vc, vv, kF32BK, p->head_dim, FLB_FP32, false);
+  const int box_rows = box_rows_for(p);
+  if (p->dtype == FLB_FP32) {   // [box_rows x D] fp32 boxes, unswizzled
+    if (int st = encode_rows_map(tmk, kc, kv, box_rows, p->head_dim, FLB_FP32, false)) return st;
+    return encode_rows_map(tmv, vc, vv, box_rows, p->head_dim, FLB_FP32, false);
   }
-  if (int st = encode_rows_x64_map(tmk, kc, kv, kDecodeBK, p->dtype)) return st;
-  return encode_rows_x64_map(tmv, vc, vv, kDecodeBK, p->dtype);
+  if (int st = encode_rows_x64_map(tmk, kc, kv, box_rows, p->dtype)) return st;
+  return encode_rows_x64_map(tmv, vc, vv, box_rows, p->dtype);
 }
 
 DecodeArgs make_args(const flb_decode_params* p) {
@@ -854,6 +917,13 @@ DecodeArgs make_args(const flb_decode_params* p) {
   a.scale_log2 = static_cast<float>(static_cast<double>(p->softmax_scale) * 1.4426950408889634);
   a.key_begin = 0;
   a.key_end = p->max_seqlen;
+  if (p->block_tables != nullptr) {
+    a.block_tables = p->block_tables;
+    a.bt_stride = p->block_table_stride;
+    a.page_size = p->page_size;
+    a.max_blocks = p->max_seqlen / p->page_size;
+  }
+  a.box_rows = box_rows_for(p);
   return a;
 }
 
@@ -1018,6 +1088,9 @@ extern "C" int flb_decode_partials(const flb_decode_params* p, int32_t key_begin
   if (key_begin < 0 || key_end < key_begin)
     return fail(FLB_ERR_INVALID_ARGUMENT, "bad key window [%d, %d)", key_begin, key_end);
   if (q.num_splits < 1) return fail(FLB_ERR_INVALID_ARGUMENT, "num_splits must be >= 1 here");
+  if (q.block_tables != nullptr && key_begin % tile_keys_for(&q) != 0)
+    return fail(FLB_ERR_UNSUPPORTED, "paged cache: key_begin %d must be a multiple of %d",
+                key_begin, tile_keys_for(&q));
   int dev = 0, sm_count = 0;
   if (int st = current_device_info(&dev, &sm_count, nullptr, nullptr)) return st;
   CUtensorMap tmk, tmv;
@@ -1119,6 +1192,9 @@ extern "C" int flb_decode_partials_push(const flb_decode_params* p, int32_t key_
     return fail(FLB_ERR_INVALID_ARGUMENT, "bad key window [%d, %d)", key_begin, key_end);
   if (q.num_splits < 1) return fail(FLB_ERR_INVALID_ARGUMENT, "num_splits must be >= 1 here");
   if (parity != 0 && parity != 1) return fail(FLB_ERR_INVALID_ARGUMENT, "parity must be 0 or 1");
+  if (q.block_tables != nullptr && key_begin % tile_keys_for(&q) != 0)
+    return fail(FLB_ERR_UNSUPPORTED, "paged cache: key_begin %d must be a multiple of %d",
+                key_begin, tile_keys_for(&q));
   int dev = 0, sm_count = 0;
   if (int st = current_device_info(&dev, &sm_count, nullptr, nullptr)) return st;
   CUtensorMap tmk, tmv;

@@ -60,6 +60,8 @@ class DecodeParams(ctypes.Structure):
         ("softmax_scale", ctypes.c_float),
         ("workspace", _p), ("workspace_bytes", ctypes.c_size_t),
         ("status", _p),
+        ("block_tables", _p), ("block_table_stride", _i64),
+        ("page_size", _i32), ("num_blocks", _i32),
     ]
 
 

@@ -68,8 +68,12 @@ class DecodeImpl:
     op: str
     dtypes: tuple
     head_dims: tuple
-    paged: bool = False
+    paged_op: str | None = None   # the op taking a block table (none: paged caches unsupported)
     in_auto: bool = True
+
+    @property
+    def paged(self) -> bool:
+        return self.paged_op is not None
 
     def unsupported_reason(self, shape: DecodeShape, dtype: torch.dtype) -> str | None:
         if dtype not in self.dtypes:
@@ -78,6 +82,8 @@ class DecodeImpl:
             return f"head_dim {shape.head_dim} is not one of {self.head_dims}"
         if shape.paged and not self.paged:
             return "paged KV caches are not supported"
+        if shape.paged and not (shape.page_size in (8, 16, 32) or shape.page_size % 64 == 0):
+            return f"page_size {shape.page_size} is not 8, 16, 32 or a multiple of 64"
         return None
 
 
@@ -89,12 +95,16 @@ PREFILL_IMPLS: dict[str, PrefillImpl] = {
                                  head_dims=(64, 128)),
 }
 DECODE_IMPLS: dict[str, DecodeImpl] = {
-    "splitkv": DecodeImpl(op="decode_splitkv", dtypes=_DECODE_DTYPES, head_dims=(64, 128)),
+    "splitkv": DecodeImpl(op="decode_splitkv", dtypes=_DECODE_DTYPES, head_dims=(64, 128),
+                          paged_op="decode_splitkv_paged"),
     "decode_inplace": DecodeImpl(op="decode_inplace", dtypes=_DECODE_DTYPES,
-                                 head_dims=(64, 128)),
+                                 head_dims=(64, 128), paged_op="decode_inplace_paged"),
 }
 
 _PREFILL_SCHEMA = "(Tensor q, Tensor k, Tensor v, bool causal, float softmax_scale) -> (Tensor, Tensor)"
+_DECODE_PAGED_SCHEMA = ("(Tensor q, Tensor k_cache, Tensor v_cache, Tensor seq_lens, "
+                        "Tensor block_tables, float softmax_scale, int num_splits) "
+                        "-> (Tensor, Tensor)")
 _DECODE_SCHEMA = ("(Tensor q, Tensor k_cache, Tensor v_cache, Tensor seq_lens, float softmax_scale,"
                   " int num_splits) -> (Tensor, Tensor)")
 
@@ -211,7 +221,7 @@ def _prefill(q, k, v, causal: bool, softmax_scale: float):
 
 
 def _decode(q, k_cache, v_cache, seq_lens, softmax_scale: float, num_splits: int,
-            allow_splits: bool):
+            allow_splits: bool, block_tables=None):
     lib = _require_library()
     if q.dtype not in _DECODE_DTYPE_CODE:
         raise RuntimeError(f"decode takes bf16, fp16 or fp32, got {q.dtype}")
@@ -220,7 +230,18 @@ def _decode(q, k_cache, v_cache, seq_lens, softmax_scale: float, num_splits: int
     if seq_lens.dtype != torch.int32 or not seq_lens.is_contiguous():
         raise RuntimeError("seq_lens must be contiguous int32")
     batch, heads, head_dim = q.shape
-    max_seqlen, heads_kv = k_cache.shape[1], k_cache.shape[2]
+    heads_kv = k_cache.shape[2]
+    if block_tables is None:
+        max_seqlen = k_cache.shape[1]
+        paged = (0, 0, 0, 0)
+    else:
+        # Paged: caches [num_blocks, page_size, H_kv, D], block_tables [B, max_blocks] int32.
+        if block_tables.dtype != torch.int32 or block_tables.dim() != 2 \
+                or block_tables.stride(1) != 1:
+            raise RuntimeError("block_tables must be [B, max_blocks] int32 with unit column stride")
+        max_seqlen = block_tables.shape[1] * k_cache.shape[1]
+        paged = (block_tables.data_ptr(), block_tables.stride(0), k_cache.shape[1],
+                 k_cache.shape[0])
     if not allow_splits:
         splits = 1
     elif num_splits > 0:
@@ -242,7 +263,7 @@ def _decode(q, k_cache, v_cache, seq_lens, softmax_scale: float, num_splits: int
         batch, heads, heads_kv, head_dim, max_seqlen, splits, _DECODE_DTYPE_CODE[q.dtype],
         float(softmax_scale),
         0 if workspace is None else workspace.data_ptr(), ws_bytes,
-        _status_ptr(q.device),
+        _status_ptr(q.device), *paged,
     )
     with _DeviceGuard(q.device):
         status = lib.flb_decode_fwd(ctypes.byref(p), torch.cuda.current_stream(q.device).cuda_stream)
@@ -256,6 +277,10 @@ def _prefill_fake(q, k, v, causal, softmax_scale):
 
 
 def _decode_fake(q, k_cache, v_cache, seq_lens, softmax_scale, num_splits):
+    return q.new_empty(q.shape), q.new_empty(q.shape[:2], dtype=torch.float32)
+
+
+def _decode_paged_fake(q, k_cache, v_cache, seq_lens, block_tables, softmax_scale, num_splits):
     return q.new_empty(q.shape), q.new_empty(q.shape[:2], dtype=torch.float32)
 
 
@@ -280,6 +305,13 @@ def _register_ops() -> None:
     _define("decode_inplace", _DECODE_SCHEMA,
             lambda q, kc, vc, sl, scale, ns: _decode(q, kc, vc, sl, scale, ns, False),
             _decode_fake)
+    # Paged-cache forms (no counterpart op in the reference, whose kernels reject block tables).
+    _define("decode_splitkv_paged", _DECODE_PAGED_SCHEMA,
+            lambda q, kc, vc, sl, bt, scale, ns: _decode(q, kc, vc, sl, scale, ns, True, bt),
+            _decode_paged_fake)
+    _define("decode_inplace_paged", _DECODE_PAGED_SCHEMA,
+            lambda q, kc, vc, sl, bt, scale, ns: _decode(q, kc, vc, sl, scale, ns, False, bt),
+            _decode_paged_fake)
 
 
 if HAS_EXTENSION:
@@ -347,8 +379,10 @@ def decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, seq_le
            impl: str = "auto", num_splits: int | None = None, return_lse: bool = False):
     """One decode step: each sequence's single query token attends to its first seq_lens[b] keys.
 
-    The cache is [B, S_max, H_kv, D], read in place through its strides. seq_lens values are not
-    checked on the host (that would force a device sync); the kernel clamps them to [0, S_max].
+    The cache is [B, S_max, H_kv, D], read in place through its strides, or paged:
+    [num_blocks, page_size, H_kv, D] with block_tables [B, max_blocks] int32 (page_size 8, 16,
+    32 or a multiple of 64). seq_lens values are not checked on the host (that would force a device
+    sync); the kernel clamps them to [0, S_max].
     num_splits=None lets the library choose the split count from the shapes only.
     """
     q3, shape = check_decode_inputs(q, k_cache, v_cache, seq_lens, block_tables)
@@ -361,8 +395,13 @@ def decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, seq_le
                  f"{shape.heads_kv}, paged={shape.paged}"),
         lambda s: s.unsupported_reason(shape, q.dtype),
     )
-    out, lse = getattr(torch.ops.flash_lab, spec.op)(q3, k_cache, v_cache, seq_lens, scale,
-                                                     num_splits or 0)
+    if block_tables is None:
+        out, lse = getattr(torch.ops.flash_lab, spec.op)(q3, k_cache, v_cache, seq_lens, scale,
+                                                         num_splits or 0)
+    else:
+        out, lse = getattr(torch.ops.flash_lab, spec.paged_op)(q3, k_cache, v_cache, seq_lens,
+                                                               block_tables, scale,
+                                                               num_splits or 0)
     if q.dim() == 4:
         out = out.unsqueeze(1)
     return (out, lse) if return_lse else out

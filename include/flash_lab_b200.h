@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define FLB_ABI_VERSION 1
+#define FLB_ABI_VERSION 2
 
 /* Most ranks a peer exchange (cross-GPU decode merge over NVLink) connects. */
 #define FLB_MAX_PEERS 8
@@ -105,6 +105,16 @@ typedef struct {
   void* workspace;
   size_t workspace_bytes;
   int32_t* status;       /* optional device status word */
+  /* Paged cache when block_tables is not NULL (the reference's paged layout, layouts.py:95-167):
+   * k_cache / v_cache are [num_blocks, page_size, H_kv, D] with k_batch_stride the block stride
+   * and k_seq_stride the row stride; key j of sequence b is row j % page_size of block
+   * block_tables[b * block_table_stride + j / page_size]; max_seqlen = max_blocks * page_size.
+   * page_size is 8, 16, 32 or a multiple of 64. Block ids outside [0, num_blocks) read as
+   * zeros. */
+  const int32_t* block_tables;
+  int64_t block_table_stride;
+  int32_t page_size;
+  int32_t num_blocks;
 } flb_decode_params;
 
 /* ABI version (FLB_ABI_VERSION). No reference counterpart. */

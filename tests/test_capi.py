@@ -39,7 +39,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_version_and_status_strings(lib):
-    assert lib.flb_version() == 1
+    assert lib.flb_version() == 2
     assert lib.flb_status_string(0) == b"ok"
     assert lib.flb_status_string(3) == b"misaligned pointer or stride"
     assert lib.flb_status_string(99) == b"unknown status"

@@ -172,7 +172,7 @@ def test_rejects_unsupported(impl):
         flash_lab.decode(q, cache, cache, seq_lens, impl=impl)
     q, cache = q[..., :64], torch.randn(4, 4, 4, 64, device="cuda", dtype=torch.bfloat16)
     tables = torch.zeros(1, 2, device="cuda", dtype=torch.int32)
-    with pytest.raises(ValueError, match="paged"):
+    with pytest.raises(ValueError, match="page_size 4"):   # pages of 4 rows: too short here
         flash_lab.decode(q.contiguous(), cache, cache, seq_lens, block_tables=tables, impl=impl)
     q64 = torch.randn(1, 1, 4, 64, device="cuda", dtype=torch.float64)
     c64 = torch.randn(1, 8, 4, 64, device="cuda", dtype=torch.float64)
@@ -225,3 +225,60 @@ def test_fp32_gqa_groups_8k(group):
                                               torch.float32, gen)
     out, lse = flash_lab.decode(q, k_cache, v_cache, seq_lens, return_lse=True)
     check_decode(out, lse, q, k_cache, v_cache, seq_lens)
+
+
+def to_paged(cache, page, perm):
+    """The same cache as a shuffled block pool [num_blocks, page, H_kv, D] (unused blocks NaN)."""
+    batch, smax, heads_kv, d = cache.shape
+    pool = torch.full((perm.numel() + 5, page, heads_kv, d), float("nan"), device=cache.device,
+                      dtype=cache.dtype)
+    pool[perm.reshape(-1)] = cache.reshape(batch * (smax // page), page, heads_kv, d)
+    return pool
+
+
+@pytest.mark.parametrize("page", [8, 16, 32, 64, 128])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32],
+                         ids=lambda d: str(d).removeprefix("torch."))
+@pytest.mark.parametrize("impl", IMPLS)
+def test_paged_cache_matches_contiguous(impl, dtype, page):
+    # The reference's paged layout (layouts.py:95-167): block_tables [B, max_blocks] int32 into a
+    # pool of pages; a shuffled pool gives bitwise the contiguous result (same keys, same splits).
+    gen = torch.Generator(device="cuda").manual_seed(30 + page)
+    q, k_cache, v_cache, seq_lens = make_case((3, 16, 4, 1024, 128, [1024, 37, 700]), dtype, gen)
+    nb = 1024 // page
+    perm = torch.randperm(3 * nb + 5, device="cuda", generator=gen)[:3 * nb].view(3, nb)
+    tables = perm.to(torch.int32)
+    kp, vp = to_paged(k_cache, page, perm), to_paged(v_cache, page, perm)
+    # Entries past each sequence's pages point at a NaN block or out of the pool: never used.
+    unused = sorted(set(range(kp.shape[0])) - set(perm.reshape(-1).tolist()))[0]
+    for b, n in enumerate(seq_lens.tolist()):
+        tables[b, -(-n // page):] = -1 if b % 2 else unused
+    ref_o, ref_lse = flash_lab.decode(q, k_cache, v_cache, seq_lens, impl=impl, return_lse=True)
+    out, lse = flash_lab.decode(q, kp, vp, seq_lens, block_tables=tables, impl=impl,
+                                return_lse=True)
+    assert torch.equal(out, ref_o) and torch.equal(lse, ref_lse)
+    check_decode(out, lse, q, k_cache, v_cache, seq_lens)
+
+
+@pytest.mark.parametrize("page", [16, 64])
+def test_paged_against_the_oracle_gqa_d64(page):
+    # head_dim 64, GQA group 4, ragged lengths: the oracle reads the pool through the tables
+    # (its gather_cache, pinned to the reference's paged golden case).
+    gen = torch.Generator(device="cuda").manual_seed(40 + page)
+    batch, heads, heads_kv, d, max_blocks = 4, 16, 4, 64, 2048 // page
+    pool_k = torch.randn(batch * max_blocks + 7, page, heads_kv, d, device="cuda",
+                         dtype=torch.bfloat16, generator=gen)
+    pool_v = torch.randn_like(pool_k)
+    tables = torch.randperm(pool_k.shape[0], device="cuda", generator=gen)[:batch * max_blocks]
+    tables = tables.view(batch, max_blocks).to(torch.int32)
+    q = torch.randn(batch, 1, heads, d, device="cuda", dtype=torch.bfloat16, generator=gen)
+    seq_lens = torch.tensor([2048, 1, 1500, 999], device="cuda", dtype=torch.int32)
+    out, lse = flash_lab.decode(q, pool_k, pool_v, seq_lens, block_tables=tables,
+                                return_lse=True)
+    ref, ref_lse = oracle.decode(host64(q), host64(pool_k), host64(pool_v),
+                                 seq_lens.cpu().numpy(), block_tables=tables.cpu().numpy(),
+                                 return_lse=True)
+    err = np.abs(host64(out) - ref).max()
+    rounding = np.abs(torch.from_numpy(ref).to(torch.bfloat16).double().numpy() - ref).max()
+    assert err <= 2 * rounding, (err, rounding)
+    assert np.abs(host64(lse) - ref_lse).max() < 1e-3
