@@ -398,22 +398,33 @@ def run_extra(torch, flash_lab, device, dist, world, rank, args, peaks, traffic)
         l2_flush.zero_()
         l2_drain.sum()
 
-    for name, (bb, hh, hk, lens_kind) in {
-        "decode_mha_32k": (8, 32, 32, "full"),
-        "decode_gqa_32k": (8, 32, 8, "ragged"),
+    # (batch, heads, heads_kv, lengths, cache dtype, page size or 0 for a contiguous cache)
+    for name, (bb, hh, hk, lens_kind, cdt, page) in {
+        "decode_mha_32k": (8, 32, 32, "full", torch.bfloat16, 0),
+        "decode_gqa_32k": (8, 32, 8, "ragged", torch.bfloat16, 0),
+        "decode_gqa_32k_paged16": (8, 32, 8, "ragged", torch.bfloat16, 16),
+        "decode_mha_32k_fp32": (4, 32, 32, "full", torch.float32, 0),
     }.items():
         smax = 32768
         gen = torch.Generator(device=device).manual_seed(7 + rank)
-        qd = torch.randn(bb, 1, hh, d, device=device, dtype=torch.bfloat16, generator=gen)
-        kc = torch.randn(bb, smax, hk, d, device=device, dtype=torch.bfloat16, generator=gen)
-        vc = torch.randn(bb, smax, hk, d, device=device, dtype=torch.bfloat16, generator=gen)
+        qd = torch.randn(bb, 1, hh, d, device=device, dtype=cdt, generator=gen)
+        kc = torch.randn(bb, smax, hk, d, device=device, dtype=cdt, generator=gen)
+        vc = torch.randn(bb, smax, hk, d, device=device, dtype=cdt, generator=gen)
+        tables = None
+        if page:
+            # The same cache as a pool of pages in a shuffled order (the reference's paged layout).
+            nb = smax // page
+            perm = torch.randperm(bb * nb, device=device, generator=gen)
+            kc = kc.view(bb * nb, page, hk, d)[torch.argsort(perm)]
+            vc = vc.view(bb * nb, page, hk, d)[torch.argsort(perm)]
+            tables = perm.view(bb, nb).to(torch.int32)
         if lens_kind == "full":
             lens = [smax] * bb
         else:
             lens = torch.randint(16384, smax + 1, (bb,),
                                  generator=torch.Generator().manual_seed(0)).tolist()
         seq_lens = torch.tensor(lens, device=device, dtype=torch.int32)
-        nbytes = decode_bytes(hh, hk, d, lens, bb)
+        nbytes = decode_bytes(hh, hk, d, lens, bb) * (2 if cdt == torch.float32 else 1)
 
         # Kernel-only time with L2 flushed before every call (flush outside the events).
         times = []
@@ -421,7 +432,7 @@ def run_extra(torch, flash_lab, device, dist, world, rank, args, peaks, traffic)
             flush_l2()
             st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             st.record()
-            flash_lab.decode(qd, kc, vc, seq_lens)
+            flash_lab.decode(qd, kc, vc, seq_lens, block_tables=tables)
             en.record()
             if i >= args.warmup:
                 times.append((st, en))
@@ -435,10 +446,12 @@ def run_extra(torch, flash_lab, device, dist, world, rank, args, peaks, traffic)
         out[name] = {"value": world * gbs, "unit": "GB/s", "ms_per_step": ms,
                      "bytes_per_call": nbytes, "roofline_frac": gbs / peaks["hbm_gbs"],
                      "peak_gbs": peaks["hbm_gbs"], "config": f"B={bb} H={hh} H_kv={hk} "
-                     f"S_max=32768 D=128 lengths={'32768' if lens_kind == 'full' else lens}",
+                     f"S_max=32768 D=128 {str(cdt).removeprefix('torch.')} "
+                     f"lengths={'32768' if lens_kind == 'full' else lens}"
+                     + (f" paged: {page}-row pages in a shuffled pool" if page else ""),
                      "l2": "512 MB buffer written, then another 512 MB read, before every "
                            "call (outside the events)"}
-        del qd, kc, vc
+        del qd, kc, vc, tables
 
     # B=1 MHA at 32K with the KV sequence split across the ranks. decode_b1_split: the peer
     # exchange (each rank's split kernel pushes its partials into every rank's buffer over

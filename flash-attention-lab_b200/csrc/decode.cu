@@ -96,10 +96,11 @@ __device__ __forceinline__ int tma_c(const TmaCoords& c, int slot, int s, int h,
 // The producer warp of both split kernels: streams ntiles tiles of kTileKeys keys (K then V) of
 // one (sequence b, KV head) starting at key k0 into the kStages ring. A tile is kColBoxes column
 // boxes (kColsPerBox columns, kColBoxBytes each in shared memory, rows of kRowBytes), each loaded
-// as kTileKeys / box_rows boxes of box_rows rows. For a paged cache each box's block comes from
-// the block table: the warp reads 32 table entries at a time (lane i holds page base + i) and
-// lane 0, which issues every copy, takes the entry it needs by shuffle. Keys past the split's end
-// are still loaded (zeros or other blocks' rows) and masked by the consumers.
+// as kTileKeys / box_rows boxes of box_rows rows; lane i issues box i of the tile, so one warp
+// instruction issues them all. For a paged cache each box's block comes from the block table:
+// the warp holds two windows of 32 entries (lane i: pages base + i and base + 32 + i), loading
+// the next window one window ahead, and each lane takes its box's entry by shuffle. Keys past
+// the split's end are still loaded (zeros or other blocks' rows) and masked by the consumers.
 template <int kTileKeys, int kColBoxes, int kColsPerBox, int kColBoxBytes, int kRowBytes,
           int kStages, int kTileBytes>
 __device__ __forceinline__ void produce_kv(const DecodeArgs& a, const CUtensorMap* tmk,
@@ -115,46 +116,52 @@ __device__ __forceinline__ void produce_kv(const DecodeArgs& a, const CUtensorMa
   }
   const bool paged = a.block_tables != nullptr;
   const int box_rows = paged ? a.box_rows : kTileKeys;
-  const int parts = kTileKeys / box_rows;
-  bool have_pages = false;
-  int page_base = 0, my_block = -1;
+  const int parts = kTileKeys / box_rows;               // boxes along the keys of one tile
+  const int boxes = 2 * parts * kColBoxes;              // K and V boxes of one tile (<= 32)
+  // This lane's box: kind (0 = K, 1 = V), part j along the keys, column box cb.
+  const int kind = lane / (parts * kColBoxes);
+  const int j = (lane / kColBoxes) % parts;
+  const int cb = lane % kColBoxes;
+  const CUtensorMap* map = kind == 0 ? tmk : tmv;
+  const TmaCoords& crd = kind == 0 ? a.kc : a.vc;
+  const int64_t bt_row = static_cast<int64_t>(b) * a.bt_stride;
+  int page_base = 0, cur = -1, next = -1;
+  if (paged) {
+    page_base = k0 / a.page_size;
+    const int p0 = page_base + lane, p1 = page_base + 32 + lane;
+    cur = p0 < a.max_blocks ? __ldg(a.block_tables + bt_row + p0) : -1;
+    next = p1 < a.max_blocks ? __ldg(a.block_tables + bt_row + p1) : -1;
+  }
   int issued = 0;
   for (int t = 0; t < ntiles; ++t) {
     const int s = t % kStages;
     bool ok = true;
     if (t >= kStages) ok = mbar_wait(&empty_bar[s], ((t / kStages) - 1) & 1, guard);
     if (!__all_sync(0xffffffffu, ok)) break;
-    uint8_t* kdst = ring + s * kStageBytes;
-    uint8_t* vdst = kdst + kTileBytes;
+    uint8_t* dst = ring + s * kStageBytes + kind * kTileBytes;
+    const int key = k0 + t * kTileKeys + j * box_rows;
+    int blk = b, row = key;
+    if (paged) {
+      // A tile spans at most 8 pages, so its pages lie in [page_base, page_base + 64).
+      if ((k0 + t * kTileKeys) / a.page_size >= page_base + 32) {
+        page_base += 32;
+        cur = next;
+        const int p1 = page_base + 32 + lane;
+        next = p1 < a.max_blocks ? __ldg(a.block_tables + bt_row + p1) : -1;
+      }
+      const int page = key / a.page_size;
+      const int idx = page - page_base;
+      const int from_cur = __shfl_sync(0xffffffffu, cur, idx & 31);
+      const int from_next = __shfl_sync(0xffffffffu, next, idx & 31);
+      blk = idx < 32 ? from_cur : from_next;
+      row = key - page * a.page_size;
+    }
     if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
-    for (int j = 0; j < parts; ++j) {
-      const int key = k0 + t * kTileKeys + j * box_rows;
-      int blk = b, row = key;
-      if (paged) {
-        const int page = key / a.page_size;
-        if (!have_pages || page >= page_base + 32) {   // pages only increase along the split
-          have_pages = true;
-          page_base = page;
-          const int p = page_base + lane;
-          my_block = p < a.max_blocks
-                         ? __ldg(a.block_tables + static_cast<int64_t>(b) * a.bt_stride + p)
-                         : -1;
-        }
-        blk = __shfl_sync(0xffffffffu, my_block, page - page_base);
-        row = key - page * a.page_size;
-      }
-      if (lane == 0) {
-#pragma unroll
-        for (int cb = 0; cb < kColBoxes; ++cb) {
-          const int off = cb * kColBoxBytes + j * box_rows * kRowBytes;
-          tma_load_4d(kdst + off, tmk, &full_bar[s], cb * kColsPerBox,
-                      tma_c(a.kc, 1, row, hkv, blk), tma_c(a.kc, 2, row, hkv, blk),
-                      tma_c(a.kc, 3, row, hkv, blk));
-          tma_load_4d(vdst + off, tmv, &full_bar[s], cb * kColsPerBox,
-                      tma_c(a.vc, 1, row, hkv, blk), tma_c(a.vc, 2, row, hkv, blk),
-                      tma_c(a.vc, 3, row, hkv, blk));
-        }
-      }
+    __syncwarp();
+    if (lane < boxes) {
+      tma_load_4d(dst + cb * kColBoxBytes + j * box_rows * kRowBytes, map, &full_bar[s],
+                  cb * kColsPerBox, tma_c(crd, 1, row, hkv, blk), tma_c(crd, 2, row, hkv, blk),
+                  tma_c(crd, 3, row, hkv, blk));
     }
     issued = t + 1;
   }
