@@ -184,9 +184,11 @@ __device__ __forceinline__ void publish_push(const DecodeArgs& a) {
   __threadfence();
   const unsigned int total = gridDim.x * gridDim.y;
   if (atomicAdd(a.cta_done, 1u) == total - 1) {
+    // One system-scope fence orders every CTA's partials before all the adds that follow
+    // (a release add per destination would fence once per destination).
     __threadfence_system();
     *a.cta_done = 0u;
-    for (int dst = 0; dst < a.n_dest; ++dst) red_release_sys_add(a.arrive[dst], 1ull);
+    for (int dst = 0; dst < a.n_dest; ++dst) red_relaxed_sys_add(a.arrive[dst], 1ull);
   }
 }
 
@@ -741,9 +743,8 @@ __global__ void decode_merge_kernel(const float* __restrict__ partial_o,
       const uint64_t start = global_timer_ns();
       for (int src = 0; src < wait.world && !failed; ++src) {
         uint32_t polls = 0;
-        while (ld_acquire_sys_u64(wait.counters + src) < wait.expected) {
-          __nanosleep(64);
-          if (((++polls) & 15u) == 0 &&
+        while (ld_relaxed_sys_u64(wait.counters + src) < wait.expected) {
+          if (((++polls) & 63u) == 0 &&
               global_timer_ns() - start > static_cast<uint64_t>(wait.timeout_ns)) {
             failed = 1;
             if (wait.status != nullptr) atomicCAS(wait.status, 0, kDevPeerTimeout);
@@ -751,6 +752,7 @@ __global__ void decode_merge_kernel(const float* __restrict__ partial_o,
           }
         }
       }
+      fence_acq_rel_sys();   // the partials the counters announce are visible from here on
       s_failed = failed;
     }
     __syncthreads();

@@ -34,16 +34,20 @@ enum DeviceStatus : int {
   kDevPeerTimeout = 2,  // another GPU's partials did not arrive in time; outputs are invalid
 };
 
-// System-scope release add (a counter another GPU polls) and acquire load (of a counter other
-// GPUs add to), for the cross-GPU decode exchange over NVLink peer memory.
-__device__ __forceinline__ void red_release_sys_add(unsigned long long* p, unsigned long long v) {
-  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+// For the cross-GPU decode exchange over NVLink peer memory: a system-scope add that an earlier
+// fence orders (release pattern), and a poll whose success is followed by one acquire fence.
+__device__ __forceinline__ void red_relaxed_sys_add(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
   unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
+}
+
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 
 // One deadline for every wait of a launch: a healthy pipeline stage completes in microseconds.
