@@ -21,8 +21,10 @@
 //    only moved (and O, l rescaled in TMEM) when a tile's max exceeds it by more than 2^8, so
 //    probabilities stay <= 256 and the common case never touches O. The final O / l and the LSE
 //    are exact for any reference point.
-//  * Causal CTAs are launched heaviest first; tiles past the diagonal are never loaded, tiles
-//    crossing it are masked element-wise.
+//  * Causal CTAs are launched heaviest first across groups of 16 (batch, head) pairs; tiles past
+//    the diagonal are never loaded, tiles crossing it are masked element-wise.
+//  * Epilogue: O / l is staged in the Q tile's shared-memory buffer (free by then) and written
+//    by TMA stores, coalesced, instead of one 256-byte row per thread.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -36,24 +38,6 @@
 #include "host_common.h"
 #include "sm100.cuh"
 
-
-// Optional phase tracing (build with -DFLB_PREFILL_TRACE): each warp accumulates clock64 cycles
-// per phase and lane 0 of every warp of two CTAs prints them at exit. Off in normal builds.
-#ifdef FLB_PREFILL_TRACE
-#include <cstdio>
-#define FLB_TRACE_DECL unsigned long long tr_[8] = {0, 0, 0, 0, 0, 0, 0, 0}; \
-  unsigned long long tr0_ = clock64(); const unsigned long long trstart_ = tr0_;
-#define FLB_TRACE(i) { const unsigned long long t1_ = clock64(); tr_[i] += t1_ - tr0_; tr0_ = t1_; }
-#define FLB_TRACE_DUMP(role)                                                                  \
-  if ((blockIdx.x == 0 || blockIdx.x == gridDim.x / 2) && lane == 0)                         \
-    printf("trace cta %d warp %d %s total %llu | %llu %llu %llu %llu %llu %llu %llu %llu\n", \
-           blockIdx.x, warp, role, clock64() - trstart_, tr_[0], tr_[1], tr_[2], tr_[3],     \
-           tr_[4], tr_[5], tr_[6], tr_[7]);
-#else
-#define FLB_TRACE_DECL
-#define FLB_TRACE(i)
-#define FLB_TRACE_DUMP(role)
-#endif
 
 namespace flb {
 namespace {
@@ -75,21 +59,14 @@ struct Geometry {
   static constexpr int kSmemData = (kQTiles + kSlots) * kTileBytes;
   static constexpr int kSmemBytes = kSmemData + 1024 + 256;
 };
-// Warps: softmax WG0 (0-3), WG1 (4-7), producer (8), MMA issuer (9). With FLB_PREFILL_REGSPLIT the
-// CTA has 12 warps and setmaxnreg moves registers from warpgroup 2 (producer, MMA, 2 spare) to
-// the softmax warpgroups: launch 168 x 3 warpgroups = 208 + 208 + 80 (+8 spare) per lane.
-#ifdef FLB_PREFILL_REGSPLIT
-constexpr int kThreads = 384;
-#else
+// Warps: softmax WG0 (0-3), WG1 (4-7), producer (8), MMA issuer (9).
 constexpr int kThreads = 320;
-#endif
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
-constexpr int kSoftmaxRegs = 208;
-constexpr int kIssueRegs = 80;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units: p <= 2^8 between rescales
 constexpr int kDefaultPolyPairs = 2;           // of every 8 score pairs, 2^x on the FMA pipe
+constexpr int kCausalGroup = 16;               // (batch, head) pairs ordered together when causal
 constexpr int kDefaultPChunks = 1;             // P published to the MMA warp in this many chunks
 
 struct PrefillArgs {
@@ -101,12 +78,12 @@ struct PrefillArgs {
   int causal, causal_offset;
   int q_blocks;
   float scale, scale_log2;
-  TmaCoords qc, kc, vc;
+  TmaCoords qc, kc, vc, oc;
 };
 
 template <int kSlots>
 struct SharedBarriers {
-  uint64_t q_full;
+  uint64_t q_full[kQTiles];
   uint64_t kv_full[kSlots];
   uint64_t kv_empty[kSlots];
   uint64_t s_full[kQTiles];
@@ -195,8 +172,8 @@ __device__ __forceinline__ void softmax_exp_store(const float* sf, float sl2, fl
 template <typename T, int D, int kPolyPairs, int kPChunks>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ PrefillArgs a, const __grid_constant__ CUtensorMap tmq,
-                   const __grid_constant__ CUtensorMap tmk,
-                   const __grid_constant__ CUtensorMap tmv) {
+                   const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                   const __grid_constant__ CUtensorMap tmo) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -209,12 +186,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Work item: the q-blocks of one (batch, head) are adjacent in launch order, so the CTAs
-  // running together share their K/V tiles in L2 (heads of one GQA group are adjacent too).
-  // Causal q-blocks run heaviest first within each head, so the last CTAs launched are light.
-  const int bh = blockIdx.x / a.q_blocks;
-  const int qrank = blockIdx.x - bh * a.q_blocks;
-  const int qb = a.causal ? (a.q_blocks - 1 - qrank) : qrank;
+  // Work item. Non-causal: the q-blocks of one (batch, head) are adjacent in launch order, so
+  // the CTAs running together share their K/V tiles in L2 (heads of one GQA group are adjacent
+  // too). Causal CTAs differ in length, so they are ordered heaviest first across groups of
+  // kCausalGroup (batch, head) pairs: all the group's last q-blocks, then the ones before, and so
+  // on. A group's K/V (33 MB at S = 4096, D = 128) stays in L2 while it runs, and the longest
+  // CTAs start well before the final wave instead of one head's length before the end.
+  int bh, qb;
+  if (a.causal) {
+    const int per_group = kCausalGroup * a.q_blocks;
+    const int g = blockIdx.x / per_group;
+    const int first = g * kCausalGroup;
+    const int width = min(kCausalGroup, a.batch * a.heads - first);   // the last group may be short
+    const int r = blockIdx.x - g * per_group;
+    bh = first + r % width;
+    qb = a.q_blocks - 1 - r / width;
+  } else {
+    bh = blockIdx.x / a.q_blocks;
+    qb = blockIdx.x - bh * a.q_blocks;
+  }
   const int b = bh / a.heads;
   const int h = bh - b * a.heads;
   const int hkv = h / a.group;
@@ -237,12 +227,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     sb->abort_flag = 0;
-    mbar_init(&sb->q_full, 1);
     for (int i = 0; i < kSlots; ++i) {
       mbar_init(&sb->kv_full[i], 1);
       mbar_init(&sb->kv_empty[i], 1);
     }
     for (int t = 0; t < kQTiles; ++t) {
+      mbar_init(&sb->q_full[t], 1);
       mbar_init(&sb->s_full[t], 1);
       mbar_init(&sb->p_half[t][0], kBM);
       mbar_init(&sb->p_half[t][1], kBM);
@@ -260,63 +250,67 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sb->tmem_base;
   const WaitGuard guard{reinterpret_cast<volatile int*>(&sb->abort_flag), a.status};
-#ifdef FLB_PREFILL_REGSPLIT
-  if (warp >= kProducerWarp) warpgroup_regs_dec<kIssueRegs>();
-#endif
   if (warp == kProducerWarp) {
     // ------------------------------- TMA producer -------------------------------
-    FLB_TRACE_DECL
     if (lane == 0 && n_kv > 0) {
       tma_prefetch_desc(&tmq);
       tma_prefetch_desc(&tmk);
       tma_prefetch_desc(&tmv);
-      mbar_arrive_expect_tx(&sb->q_full, kQTiles * kTileBytes);
-      for (int t = 0; t < kQTiles; ++t) {
-        load_tile<D>(q_smem + t * kTileBytes, &tmq, a.qc, &sb->q_full, q0 + t * kBM, h, b);
-      }
+      tma_prefetch_desc(&tmo);
+      // Q tile 0 and K_0 go first, so tile 0's first Q K^T waits for 64 KB instead of 96 KB.
+      // A Q tile without keys is never loaded: its buffer is where its warpgroup stages O.
+      auto load_q = [&](int t) {
+        if (n_kv_tile[t] == 0) return;
+        mbar_arrive_expect_tx(&sb->q_full[t], kTileBytes);
+        load_tile<D>(q_smem + t * kTileBytes, &tmq, a.qc, &sb->q_full[t], q0 + t * kBM, h, b);
+      };
+      load_q(0);
       int issued = 0;
       bool ok = true;
       for (int j = 0; j < n_kv && ok; ++j) {
         for (int kind = 0; kind < 2; ++kind) {
           const int i = 2 * j + kind;
           const int slot = i % kSlots;
-          FLB_TRACE(1)
           if (i >= kSlots && !mbar_wait(&sb->kv_empty[slot], ((i / kSlots) - 1) & 1, guard)) {
             ok = false;
             break;
           }
-          FLB_TRACE(0)
           mbar_arrive_expect_tx(&sb->kv_full[slot], kTileBytes);
           load_tile<D>(ring + slot * kTileBytes, kind == 0 ? &tmk : &tmv, kind == 0 ? a.kc : a.vc,
                     &sb->kv_full[slot], j * kBN, hkv, b);
           issued = i + 1;
+          if (i == 0) {
+            for (int t = 1; t < kQTiles; ++t) load_q(t);
+          }
         }
       }
-      // Wait for the copies still landing before the CTA may exit.
-      mbar_wait(&sb->q_full, 0, guard);
+      // Wait for the copies still landing before the CTA may exit (the other Q tiles were
+      // issued right after K_0, the first ring copy, which needs no wait).
+      for (int t = 0; t < kQTiles; ++t) {
+        if (n_kv_tile[t] > 0) mbar_wait(&sb->q_full[t], 0, guard);
+      }
       for (int i = issued > kSlots ? issued - kSlots : 0; i < issued; ++i) {
         if (!mbar_wait(&sb->kv_full[i % kSlots], (i / kSlots) & 1, guard)) break;
       }
     }
-    FLB_TRACE_DUMP("producer(0=wait_empty,1=issue)")
   } else if (warp == kMmaWarp) {
     // ------------------------------- MMA issuer -------------------------------
     // The whole warp runs this loop (waits and descriptors stay warp-uniform); elect.sync picks
     // the one lane that issues each tcgen05.mma / commit.
-    FLB_TRACE_DECL
     if (n_kv > 0) {
       constexpr int kFmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
       constexpr uint32_t kIdescQK = umma_idesc_f16(kFmt, kBM, kBN, 0);
       constexpr uint32_t kIdescPV = umma_idesc_f16(kFmt, kBM, D, 1);
       const uint32_t q_addr = smem_u32(q_smem);
       const uint32_t ring_addr = smem_u32(ring);
-      bool ok = mbar_wait(&sb->q_full, 0, guard) && mbar_wait(&sb->kv_full[0], 0, guard);
-      ok = __all_sync(0xffffffffu, ok);
+      bool ok = __all_sync(0xffffffffu, mbar_wait(&sb->kv_full[0], 0, guard));
       if (ok) {
-        tc_fence_after();
 #pragma unroll
         for (int t = 0; t < kQTiles; ++t) {
           if (n_kv_tile[t] == 0) continue;
+          ok = __all_sync(0xffffffffu, mbar_wait(&sb->q_full[t], 0, guard));
+          if (!ok) break;
+          tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             umma_ss_elect(tmem + t * 128, kmajor_desc(q_addr + t * kTileBytes, kk),
@@ -324,17 +318,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           umma_commit_elect(&sb->s_full[t]);
         }
-        umma_commit_elect(&sb->kv_empty[0]);
+        if (ok) umma_commit_elect(&sb->kv_empty[0]);
       }
       for (int j = 0; j < n_kv && ok; ++j) {
         const int iv = 2 * j + 1;  // V_j ring index
         const int sv = iv % kSlots;
         const int ik = 2 * j + 2;  // K_{j+1} ring index
         const int sk = ik % kSlots;
-        FLB_TRACE(2)
         ok = __all_sync(0xffffffffu, mbar_wait(&sb->kv_full[sv], (iv / kSlots) & 1, guard));
         if (!ok) break;
-        FLB_TRACE(0)
         const uint32_t v_addr = ring_addr + sv * kTileBytes;
         const uint32_t k_addr = ring_addr + sk * kTileBytes;
         bool k_ready = false;
@@ -347,7 +339,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int ch = 0; ch < kPChunks; ++ch) {
               ok = __all_sync(0xffffffffu, mbar_wait(&sb->p_half[t][ch], j & 1, guard));
               if (!ok) break;
-              FLB_TRACE(1)
               tc_fence_after();
 #pragma unroll
               for (int kq = 0; kq < kBN / 16 / kPChunks; ++kq) {
@@ -383,14 +374,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Every MMA issued has completed before TMEM may be released.
       umma_commit_elect(&sb->mma_done);
       mbar_wait(&sb->mma_done, 0, guard);
-      FLB_TRACE(3)
     }
-    FLB_TRACE_DUMP("mma(0=wait_kv,1=wait_p,2=issue,3=drain)")
   } else if (warp < kProducerWarp) {
     // ------------------------------- softmax warpgroups -------------------------------
-#ifdef FLB_PREFILL_REGSPLIT
-    warpgroup_regs_inc<kSoftmaxRegs>();
-#endif
     const int t = warp >> 2;                  // Q tile of this warpgroup
     const int quarter = warp & 3;             // TMEM lane quarter this warp may access
     const int row_in_tile = quarter * 32 + lane;
@@ -404,15 +390,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     float m_ref = -INFINITY;  // log2-domain reference point of this row
     float l_sum = 0.f;
     bool ok = true;
-    FLB_TRACE_DECL
     const int n_kv_t = n_kv_tile[t];
     for (int j = 0; j < n_kv_t; ++j) {
-      FLB_TRACE(6)
       if (!mbar_wait(&sb->s_full[t], j & 1, guard)) {
         ok = false;
         break;
       }
-      FLB_TRACE(0)
       tc_fence_after();
       uint32_t s[128];
       tmem_ld32(taddr_s + 0, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
@@ -420,7 +403,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld32(taddr_s + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
       tmem_ld32(taddr_s + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
       tmem_ld_wait();
-      FLB_TRACE(1)
       float* sf = reinterpret_cast<float*>(s);
 
       const int k0 = j * kBN;
@@ -477,26 +459,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       // warp in kPChunks chunks as soon as each chunk is in TMEM.
       float ps[4] = {0.f, 0.f, 0.f, 0.f};
       const float nref = -ref;
-      FLB_TRACE(2)
       if (tile_needs_mask) {
         softmax_exp_store<T, 0, kPChunks>(sf, sl2, nref, ps, taddr_s, sb->p_half[t]);
       } else {
         softmax_exp_store<T, kPolyPairs, kPChunks>(sf, sl2, nref, ps, taddr_s, sb->p_half[t]);
       }
       l_sum += (ps[0] + ps[1]) + (ps[2] + ps[3]);
-      FLB_TRACE(3)
-      FLB_TRACE(4)
     }
 
-    // Epilogue: O / l in the input dtype, and the natural-log LSE.
+    // Epilogue: O / l in the input dtype, staged in this Q tile's shared-memory buffer (free:
+    // o_full follows every MMA of the tile, its Q K^T included) in the Q tile's swizzled layout,
+    // then written by TMA stores, which clip rows past S_q; and the natural-log LSE.
     if (ok && n_kv_t > 0) ok = mbar_wait(&sb->o_full[t], 0, guard);
+    uint8_t* stage = q_smem + t * kTileBytes;
     if (ok) {
       tc_fence_after();
-      const bool row_ok = row < a.seqlen_q;
       const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
-      T* orow = static_cast<T*>(a.o) + static_cast<int64_t>(b) * a.o_batch_stride +
-                static_cast<int64_t>(row) * a.o_seq_stride +
-                static_cast<int64_t>(h) * a.o_head_stride;
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
         uint32_t ov[32];
@@ -507,20 +485,31 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 32; ++e) ov[e] = 0u;
         }
-        if (row_ok) {
-          const float* of = reinterpret_cast<const float*>(ov);
-          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+        const float* of = reinterpret_cast<const float*>(ov);
 #pragma unroll
-          for (int v = 0; v < 4; ++v) dst[v] = pack8<T>(of + 8 * v, inv);
+        for (int v = 0; v < 4; ++v) {
+          const int chunk = c * 4 + v;      // 16-byte chunk of the row: 8 per 64-column box
+          *reinterpret_cast<uint4*>(stage + (chunk >> 3) * kBoxBytes + sw128_offset(
+              static_cast<uint32_t>(row_in_tile), static_cast<uint32_t>(chunk & 7))) =
+              pack8<T>(of + 8 * v, inv);
         }
       }
-      if (row_ok) {
+      fence_proxy_async_shared();
+      if (row < a.seqlen_q) {
         a.lse[(static_cast<int64_t>(b) * a.heads + h) * a.seqlen_q + row] =
             l_sum > 0.f ? m_ref * 0.69314718055994530942f + logf(l_sum) : -INFINITY;
       }
     }
-    FLB_TRACE(5)
-    FLB_TRACE_DUMP("softmax(0=wait_s,1=ld,2=max+rescale,3=exp+st,4=-,5=epilogue,6=loop)")
+    asm volatile("bar.sync %0, 128;" ::"r"(1 + t) : "memory");   // this warpgroup only
+    if (threadIdx.x % 128 == 0 && ok && !sb->abort_flag) {
+#pragma unroll
+      for (int box = 0; box < D / 64; ++box) {
+        tma_store_4d(&tmo, stage + box * kBoxBytes, box * 64, tma_c(a.oc, 1, tile_row0, h, b),
+                     tma_c(a.oc, 2, tile_row0, h, b), tma_c(a.oc, 3, tile_row0, h, b));
+      }
+      tma_store_commit();
+      tma_store_wait_read();   // the CTA may exit once the stores have read the stage
+    }
   }
 
   tc_fence_before();
@@ -531,10 +520,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// The four tensor maps of a launch: q, k, v loads and the o store.
+struct Maps {
+  CUtensorMap q, k, v, o;
+};
+
 // One shared-memory opt-in per (kernel instantiation, device) and host thread.
 template <typename T, int D, int kPoly, int kChunks>
-int launch_variant(const PrefillArgs& a, const CUtensorMap& tmq, const CUtensorMap& tmk,
-                   const CUtensorMap& tmv, int grid, int dev, cudaStream_t stream) {
+int launch_variant(const PrefillArgs& a, const Maps& m, int grid, int dev, cudaStream_t stream) {
   constexpr int kSmemBytes = Geometry<D>::kSmemBytes;
   static thread_local int configured_device = -1;
   if (configured_device != dev) {
@@ -545,7 +538,7 @@ int launch_variant(const PrefillArgs& a, const CUtensorMap& tmq, const CUtensorM
       return st;
     configured_device = dev;
   }
-  prefill_kernel<T, D, kPoly, kChunks><<<grid, kThreads, kSmemBytes, stream>>>(a, tmq, tmk, tmv);
+  prefill_kernel<T, D, kPoly, kChunks><<<grid, kThreads, kSmemBytes, stream>>>(a, m.q, m.k, m.v, m.o);
   return check_cuda(cudaGetLastError(), "prefill_kernel launch");
 }
 
@@ -569,26 +562,24 @@ int p_chunks() {
 }
 
 template <typename T, int kChunks>
-int launch_poly(const PrefillArgs& a, const CUtensorMap& tmq, const CUtensorMap& tmk,
-                const CUtensorMap& tmv, int grid, int dev, cudaStream_t stream) {
+int launch_poly(const PrefillArgs& a, const Maps& m, int grid, int dev, cudaStream_t stream) {
   switch (poly_pairs()) {
-    case 0: return launch_variant<T, 128, 0, kChunks>(a, tmq, tmk, tmv, grid, dev, stream);
-    case 2: return launch_variant<T, 128, 2, kChunks>(a, tmq, tmk, tmv, grid, dev, stream);
-    case 3: return launch_variant<T, 128, 3, kChunks>(a, tmq, tmk, tmv, grid, dev, stream);
-    default: return launch_variant<T, 128, 4, kChunks>(a, tmq, tmk, tmv, grid, dev, stream);
+    case 0: return launch_variant<T, 128, 0, kChunks>(a, m, grid, dev, stream);
+    case 2: return launch_variant<T, 128, 2, kChunks>(a, m, grid, dev, stream);
+    case 3: return launch_variant<T, 128, 3, kChunks>(a, m, grid, dev, stream);
+    default: return launch_variant<T, 128, 4, kChunks>(a, m, grid, dev, stream);
   }
 }
 
 // head_dim 128 takes the tuning knobs; head_dim 64 runs the default variant.
 template <typename T>
-int launch_prefill(const PrefillArgs& a, const CUtensorMap& tmq, const CUtensorMap& tmk,
-                   const CUtensorMap& tmv, int head_dim, int grid, int dev, cudaStream_t stream) {
+int launch_prefill(const PrefillArgs& a, const Maps& m, int head_dim, int grid, int dev, cudaStream_t stream) {
   if (head_dim == 64) {
-    return launch_variant<T, 64, kDefaultPolyPairs, kDefaultPChunks>(a, tmq, tmk, tmv, grid, dev,
+    return launch_variant<T, 64, kDefaultPolyPairs, kDefaultPChunks>(a, m, grid, dev,
                                                                      stream);
   }
-  if (p_chunks() == 1) return launch_poly<T, 1>(a, tmq, tmk, tmv, grid, dev, stream);
-  return launch_poly<T, 2>(a, tmq, tmk, tmv, grid, dev, stream);
+  if (p_chunks() == 1) return launch_poly<T, 1>(a, m, grid, dev, stream);
+  return launch_poly<T, 2>(a, m, grid, dev, stream);
 }
 
 int validate(const flb_attn_params* p) {
@@ -636,7 +627,7 @@ extern "C" int flb_prefill_fwd(const flb_attn_params* p, flb_stream_t stream_) {
            {p->k_batch_stride, p->k_seq_stride, p->k_head_stride, 1}, 2};
   View4 vv{p->v, {p->batch, p->seqlen_k, p->heads_kv, p->head_dim},
            {p->v_batch_stride, p->v_seq_stride, p->v_head_stride, 1}, 2};
-  CUtensorMap tmq, tmk, tmv;
+  Maps m;
   PrefillArgs a{};
   if (!rows_16b_aligned(qv))
     return fail(FLB_ERR_MISALIGNED, "q must have 16-byte aligned rows (data pointer and strides)");
@@ -644,9 +635,12 @@ extern "C" int flb_prefill_fwd(const flb_attn_params* p, flb_stream_t stream_) {
     return fail(FLB_ERR_MISALIGNED, "k must have 16-byte aligned rows (data pointer and strides)");
   if (!rows_16b_aligned(vv))
     return fail(FLB_ERR_MISALIGNED, "v must have 16-byte aligned rows (data pointer and strides)");
-  if (int st = encode_rows_x64_map(&tmq, &a.qc, qv, kBM, p->dtype)) return st;
-  if (int st = encode_rows_x64_map(&tmk, &a.kc, kv, kBN, p->dtype)) return st;
-  if (int st = encode_rows_x64_map(&tmv, &a.vc, vv, kBN, p->dtype)) return st;
+  View4 ov{p->o, {p->batch, p->seqlen_q, p->heads, p->head_dim},
+           {p->o_batch_stride, p->o_seq_stride, p->o_head_stride, 1}, 2};
+  if (int st = encode_rows_x64_map(&m.q, &a.qc, qv, kBM, p->dtype)) return st;
+  if (int st = encode_rows_x64_map(&m.k, &a.kc, kv, kBN, p->dtype)) return st;
+  if (int st = encode_rows_x64_map(&m.v, &a.vc, vv, kBN, p->dtype)) return st;
+  if (int st = encode_rows_x64_map(&m.o, &a.oc, ov, kBM, p->dtype)) return st;
 
   a.o = p->o;
   a.lse = p->lse;
@@ -669,6 +663,6 @@ extern "C" int flb_prefill_fwd(const flb_attn_params* p, flb_stream_t stream_) {
   const int grid = a.q_blocks * p->batch * p->heads;
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   if (p->dtype == FLB_BF16)
-    return launch_prefill<__nv_bfloat16>(a, tmq, tmk, tmv, p->head_dim, grid, dev, stream);
-  return launch_prefill<__half>(a, tmq, tmk, tmv, p->head_dim, grid, dev, stream);
+    return launch_prefill<__nv_bfloat16>(a, m, p->head_dim, grid, dev, stream);
+  return launch_prefill<__half>(a, m, p->head_dim, grid, dev, stream);
 }
