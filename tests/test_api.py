@@ -145,3 +145,21 @@ def test_fake_kernels_give_output_shapes():
         lens = torch.empty(2, dtype=torch.int32, device="cuda")
         o, lse = torch.ops.flash_lab.decode_splitkv(q3, cache, cache, lens, 0.1, 0)
         assert o.shape == q3.shape and lse.shape == (2, 8)
+
+
+def test_c_abi_error_status_becomes_runtime_error(monkeypatch):
+    # An error status from the library (here a fake one) reaches Python as RuntimeError with the
+    # library's message, as the reference's TORCH_CHECK failures did.
+    from flash_lab import _capi, ops
+
+    class FakeLib:
+        def flb_last_error(self):
+            return b"injected launch failure"
+
+        def flb_status_string(self, status):
+            return b"CUDA error"
+
+    monkeypatch.setattr(ops, "_LIB", FakeLib())
+    with pytest.raises(RuntimeError, match="flb_decode_fwd: CUDA error: injected launch failure"):
+        ops._check(_capi.FLB_ERR_CUDA, "flb_decode_fwd", torch.device("cpu"))
+    ops._check(_capi.FLB_OK, "flb_decode_fwd", torch.device("cpu"))   # OK passes silently

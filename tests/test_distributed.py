@@ -326,3 +326,51 @@ def test_two_gpus_over_peer_memory():
     for p in procs:
         p.join(timeout=300)
         assert p.exitcode == 0
+
+
+def _dropout_rank(rank, world, port, results):
+    # Rank 1 fails on the host before the step (an exception in its own code); rank 0 enters
+    # decode_sharded and must get an error from the process group's timeout, not hang.
+    import datetime
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=4))
+    try:
+        if rank == 1:
+            results[rank] = "raised"
+            raise RuntimeError("injected failure on rank 1")
+        gen = torch.Generator().manual_seed(0)
+        q = torch.randn(1, 4, 16, generator=gen, dtype=torch.float64)
+        kc = torch.randn(1, 64, 2, 16, generator=gen, dtype=torch.float64)
+        lens = torch.tensor([64], dtype=torch.int32)
+        shard = ShardSpec.even(64, world, rank)
+        try:
+            decode_sharded(q, kc[:, :shard.length], kc[:, :shard.length], lens, shard,
+                           _partials=numpy_partials, _merge=numpy_merge)
+            results[rank] = "returned"
+        except Exception as exc:  # the collective's timeout or the peer's disconnect
+            results[rank] = f"error: {type(exc).__name__}"
+    except RuntimeError:
+        pass
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def test_rank_dropout_ends_the_step_with_an_error():
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as manager:
+        results = manager.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_dropout_rank, args=(r, 2, port, results)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=120)
+            assert p.exitcode is not None, "a rank hung"
+        out = dict(results)
+    assert out[1] == "raised"
+    assert out[0].startswith("error"), out
