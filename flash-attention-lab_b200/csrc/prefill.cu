@@ -21,15 +21,25 @@
 //    only moved (and O, l rescaled in TMEM) when a tile's max exceeds it by more than 2^8, so
 //    probabilities stay <= 256 and the common case never touches O. The final O / l and the LSE
 //    are exact for any reference point.
-//  * Causal CTAs are launched heaviest first across groups of 16 (batch, head) pairs; tiles past
-//    the diagonal are never loaded, tiles crossing it are masked element-wise.
-//  * Epilogue: O / l is staged in the Q tile's shared-memory buffer (free by then) and written
-//    by TMA stores, coalesced, instead of one 256-byte row per thread.
+//  * Work items are 256 query rows of one (batch, head). Two launch forms of one kernel:
+//    - one item per CTA (head_dim 128): non-causal q-blocks of one (batch, head) are adjacent in
+//      launch order, so the CTAs running together share K/V in L2; causal CTAs run heaviest
+//      first across groups of 16 (batch, head) pairs. The epilogue stages O / l in the Q tile's
+//      shared-memory buffer (free by then) and writes it with TMA stores.
+//    - persistent CTAs, one per SM, each running a fixed sequence of items (head_dim 64, where
+//      the per-item start and end weigh more against the shorter GEMMs). Barrier phases continue
+//      across items; the next item's Q tiles load as soon as the last Q K^T reading them
+//      completes and its K/V tiles stream on through the same ring. Causal work comes in units
+//      of two q-blocks of one head, the i-th heaviest with the i-th lightest, so every unit
+//      costs the same and the static assignment stays balanced. The Q buffers are not free for
+//      staging here, so each softmax thread stores its O row directly.
+//  * Tiles past the diagonal are never loaded; tiles crossing it are masked element-wise.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstdlib>
@@ -66,8 +76,9 @@ constexpr int kMmaWarp = 9;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units: p <= 2^8 between rescales
 constexpr int kDefaultPolyPairs = 2;           // of every 8 score pairs, 2^x on the FMA pipe
-constexpr int kCausalGroup = 16;               // (batch, head) pairs ordered together when causal
 constexpr int kDefaultPChunks = 1;             // P published to the MMA warp in this many chunks
+constexpr int kCausalGroup = 16;               // (batch, head) pairs ordered together (one item
+                                               // per CTA, causal)
 
 struct PrefillArgs {
   void* o;
@@ -84,6 +95,7 @@ struct PrefillArgs {
 template <int kSlots>
 struct SharedBarriers {
   uint64_t q_full[kQTiles];
+  uint64_t q_free[kQTiles];      // the last Q K^T of an item that reads a Q buffer has completed
   uint64_t kv_full[kSlots];
   uint64_t kv_empty[kSlots];
   uint64_t s_full[kQTiles];
@@ -169,7 +181,70 @@ __device__ __forceinline__ void softmax_exp_store(const float* sf, float sl2, fl
   }
 }
 
-template <typename T, int D, int kPolyPairs, int kPChunks>
+// Work item k of this CTA: a (batch * head, q-block) pair, or nothing past the end. Every role
+// walks the same sequence.
+//  One item per CTA: item 0 only. Non-causal in launch order (the q-blocks of one (batch, head)
+//  adjacent: they share K/V in L2). Causal heaviest first across groups of kCausalGroup (batch,
+//  head) pairs: all the group's last q-blocks, then the ones before, and so on; a group's K/V
+//  (33 MB at S = 4096, D = 128) stays in L2 while it runs, and the longest CTAs start well
+//  before the final wave.
+//  Persistent: non-causal, CTA c takes items c, c + grid, ... in launch order. Causal, the unit
+//  of work is a pair of q-blocks of one (batch, head), the i-th heaviest and the i-th lightest,
+//  whose costs add up to the same total for every pair; CTA c takes units c, c + grid, ... and
+//  runs the heavy item of each unit first.
+struct Item {
+  int bh, qb;
+};
+
+template <bool kPersistent>
+__device__ __forceinline__ bool item_at(const PrefillArgs& a, int k, Item& it) {
+  if (!kPersistent) {
+    if (k > 0) return false;
+    if (a.causal) {
+      const int per_group = kCausalGroup * a.q_blocks;
+      const int g = blockIdx.x / per_group;
+      const int first = g * kCausalGroup;
+      const int width = min(kCausalGroup, a.batch * a.heads - first);   // last group may be short
+      const int r = blockIdx.x - g * per_group;
+      it.bh = first + r % width;
+      it.qb = a.q_blocks - 1 - r / width;
+    } else {
+      it.bh = blockIdx.x / a.q_blocks;
+      it.qb = blockIdx.x - it.bh * a.q_blocks;
+    }
+    return true;
+  }
+  if (!a.causal) {
+    const int64_t u = blockIdx.x + static_cast<int64_t>(k) * gridDim.x;
+    if (u >= static_cast<int64_t>(a.batch) * a.heads * a.q_blocks) return false;
+    it.bh = static_cast<int>(u / a.q_blocks);
+    it.qb = static_cast<int>(u - static_cast<int64_t>(it.bh) * a.q_blocks);
+    return true;
+  }
+  const int pairs = (a.q_blocks + 1) / 2;
+  // Items per round: every CTA runs one unit per round, each unit 2 items (the middle q-block
+  // of an odd count is a unit of 1, whose second item is skipped).
+  const int round = k >> 1, sub = k & 1;
+  const int64_t u = blockIdx.x + static_cast<int64_t>(round) * gridDim.x;
+  if (u >= static_cast<int64_t>(a.batch) * a.heads * pairs) return false;
+  it.bh = static_cast<int>(u / pairs);
+  const int p = static_cast<int>(u - static_cast<int64_t>(it.bh) * pairs);
+  it.qb = sub == 0 ? a.q_blocks - 1 - p : p;
+  if (sub == 1 && it.qb == a.q_blocks - 1 - p) it.qb = -1;   // single-item unit
+  return true;
+}
+
+// KV tiles each Q tile of an item needs: all of them, or up to the last key its last row sees
+// (causal). The item streams the larger count; Q tile 0 of a causal item stops earlier.
+__device__ __forceinline__ int kv_tiles_for(const PrefillArgs& a, int qb, int t) {
+  const int kv_tiles_all = (a.seqlen_k + kBN - 1) / kBN;
+  if (!a.causal) return kv_tiles_all;
+  const int last_row = min(qb * kRowsPerCta + (t + 1) * kBM, a.seqlen_q) - 1;
+  const int max_key = last_row + a.causal_offset;  // last key any row of the tile sees
+  return max_key < 0 ? 0 : min(kv_tiles_all, max_key / kBN + 1);
+}
+
+template <typename T, int D, int kPolyPairs, int kPChunks, bool kPersistent>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_kernel(const __grid_constant__ PrefillArgs a, const __grid_constant__ CUtensorMap tmq,
                    const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
@@ -186,45 +261,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Work item. Non-causal: the q-blocks of one (batch, head) are adjacent in launch order, so
-  // the CTAs running together share their K/V tiles in L2 (heads of one GQA group are adjacent
-  // too). Causal CTAs differ in length, so they are ordered heaviest first across groups of
-  // kCausalGroup (batch, head) pairs: all the group's last q-blocks, then the ones before, and so
-  // on. A group's K/V (33 MB at S = 4096, D = 128) stays in L2 while it runs, and the longest
-  // CTAs start well before the final wave instead of one head's length before the end.
-  int bh, qb;
-  if (a.causal) {
-    const int per_group = kCausalGroup * a.q_blocks;
-    const int g = blockIdx.x / per_group;
-    const int first = g * kCausalGroup;
-    const int width = min(kCausalGroup, a.batch * a.heads - first);   // the last group may be short
-    const int r = blockIdx.x - g * per_group;
-    bh = first + r % width;
-    qb = a.q_blocks - 1 - r / width;
-  } else {
-    bh = blockIdx.x / a.q_blocks;
-    qb = blockIdx.x - bh * a.q_blocks;
-  }
-  const int b = bh / a.heads;
-  const int h = bh - b * a.heads;
-  const int hkv = h / a.group;
-  const int q0 = qb * kRowsPerCta;
-
-  // KV tiles each Q tile needs: all of them, or up to the last key its last row sees (causal).
-  // The CTA streams the larger count; Q tile 0 of a causal CTA stops earlier.
-  const int kv_tiles_all = (a.seqlen_k + kBN - 1) / kBN;
-  int n_kv_tile[kQTiles];
-#pragma unroll
-  for (int t = 0; t < kQTiles; ++t) {
-    n_kv_tile[t] = kv_tiles_all;
-    if (a.causal) {
-      const int last_row = min(q0 + (t + 1) * kBM, a.seqlen_q) - 1;
-      const int max_key = last_row + a.causal_offset;  // last key any row of the tile sees
-      n_kv_tile[t] = max_key < 0 ? 0 : min(kv_tiles_all, max_key / kBN + 1);
-    }
-  }
-  const int n_kv = max(n_kv_tile[0], n_kv_tile[1]);
-
   if (threadIdx.x == 0) {
     sb->abort_flag = 0;
     for (int i = 0; i < kSlots; ++i) {
@@ -233,6 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int t = 0; t < kQTiles; ++t) {
       mbar_init(&sb->q_full[t], 1);
+      mbar_init(&sb->q_free[t], 1);
       mbar_init(&sb->s_full[t], 1);
       mbar_init(&sb->p_half[t][0], kBM);
       mbar_init(&sb->p_half[t][1], kBM);
@@ -250,44 +287,64 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = sb->tmem_base;
   const WaitGuard guard{reinterpret_cast<volatile int*>(&sb->abort_flag), a.status};
+
+  // Barrier phases run on across items: each role counts the completions it has waited for.
   if (warp == kProducerWarp) {
     // ------------------------------- TMA producer -------------------------------
-    if (lane == 0 && n_kv > 0) {
+    // Per item: Q tile 0, K_0, Q tile 1, V_0, K_1, V_1, ... (Q tile 0 and K_0 first, so tile 0's
+    // first Q K^T waits for 64 KB). A Q buffer is reloaded for the next item as soon as the last
+    // Q K^T of the previous item that reads it has completed (q_free), which is while that
+    // item's last tiles still run. Q tiles without keys are not loaded.
+    if (lane == 0) {
       tma_prefetch_desc(&tmq);
       tma_prefetch_desc(&tmk);
       tma_prefetch_desc(&tmv);
-      tma_prefetch_desc(&tmo);
-      // Q tile 0 and K_0 go first, so tile 0's first Q K^T waits for 64 KB instead of 96 KB.
-      // A Q tile without keys is never loaded: its buffer is where its warpgroup stages O.
-      auto load_q = [&](int t) {
-        if (n_kv_tile[t] == 0) return;
-        mbar_arrive_expect_tx(&sb->q_full[t], kTileBytes);
-        load_tile<D>(q_smem + t * kTileBytes, &tmq, a.qc, &sb->q_full[t], q0 + t * kBM, h, b);
-      };
-      load_q(0);
-      int issued = 0;
+      if (!kPersistent) tma_prefetch_desc(&tmo);
+      int issued = 0;                  // ring copies issued (K and V tiles, all items)
+      int q_loads[kQTiles] = {};       // Q copies issued per buffer
       bool ok = true;
-      for (int j = 0; j < n_kv && ok; ++j) {
-        for (int kind = 0; kind < 2; ++kind) {
-          const int i = 2 * j + kind;
-          const int slot = i % kSlots;
-          if (i >= kSlots && !mbar_wait(&sb->kv_empty[slot], ((i / kSlots) - 1) & 1, guard)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&sb->kv_full[slot], kTileBytes);
-          load_tile<D>(ring + slot * kTileBytes, kind == 0 ? &tmk : &tmv, kind == 0 ? a.kc : a.vc,
-                    &sb->kv_full[slot], j * kBN, hkv, b);
-          issued = i + 1;
-          if (i == 0) {
-            for (int t = 1; t < kQTiles; ++t) load_q(t);
+      Item it;
+      for (int k = 0; ok && item_at<kPersistent>(a, k, it); ++k) {
+        if (it.qb < 0) continue;
+        const int b = it.bh / a.heads, h = it.bh - b * a.heads, hkv = h / a.group;
+        const int q0 = it.qb * kRowsPerCta;
+        int n_kv_tile[kQTiles];
+#pragma unroll
+        for (int t = 0; t < kQTiles; ++t) n_kv_tile[t] = kv_tiles_for(a, it.qb, t);
+        const int n_kv = n_kv_tile[kQTiles - 1];
+        if (n_kv == 0) continue;
+        auto load_q = [&](int t) -> bool {
+          if (n_kv_tile[t] == 0) return true;
+          if (kPersistent && q_loads[t] > 0 &&
+              !mbar_wait(&sb->q_free[t], (q_loads[t] - 1) & 1, guard))
+            return false;
+          mbar_arrive_expect_tx(&sb->q_full[t], kTileBytes);
+          load_tile<D>(q_smem + t * kTileBytes, &tmq, a.qc, &sb->q_full[t], q0 + t * kBM, h, b);
+          ++q_loads[t];
+          return true;
+        };
+        ok = load_q(0);
+        for (int j = 0; j < n_kv && ok; ++j) {
+          for (int kind = 0; kind < 2 && ok; ++kind) {
+            const int i = issued;
+            const int slot = i % kSlots;
+            if (i >= kSlots && !mbar_wait(&sb->kv_empty[slot], ((i / kSlots) - 1) & 1, guard)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&sb->kv_full[slot], kTileBytes);
+            load_tile<D>(ring + slot * kTileBytes, kind == 0 ? &tmk : &tmv,
+                         kind == 0 ? a.kc : a.vc, &sb->kv_full[slot], j * kBN, hkv, b);
+            ++issued;
+            if (j == 0 && kind == 0) {
+              for (int t = 1; t < kQTiles && ok; ++t) ok = load_q(t);
+            }
           }
         }
       }
-      // Wait for the copies still landing before the CTA may exit (the other Q tiles were
-      // issued right after K_0, the first ring copy, which needs no wait).
+      // Wait for the copies still landing before the CTA may exit.
       for (int t = 0; t < kQTiles; ++t) {
-        if (n_kv_tile[t] > 0) mbar_wait(&sb->q_full[t], 0, guard);
+        if (q_loads[t] > 0) mbar_wait(&sb->q_full[t], (q_loads[t] - 1) & 1, guard);
       }
       for (int i = issued > kSlots ? issued - kSlots : 0; i < issued; ++i) {
         if (!mbar_wait(&sb->kv_full[i % kSlots], (i / kSlots) & 1, guard)) break;
@@ -296,36 +353,62 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kMmaWarp) {
     // ------------------------------- MMA issuer -------------------------------
     // The whole warp runs this loop (waits and descriptors stay warp-uniform); elect.sync picks
-    // the one lane that issues each tcgen05.mma / commit.
-    if (n_kv > 0) {
-      constexpr int kFmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
-      constexpr uint32_t kIdescQK = umma_idesc_f16(kFmt, kBM, kBN, 0);
-      constexpr uint32_t kIdescPV = umma_idesc_f16(kFmt, kBM, D, 1);
-      const uint32_t q_addr = smem_u32(q_smem);
-      const uint32_t ring_addr = smem_u32(ring);
-      bool ok = __all_sync(0xffffffffu, mbar_wait(&sb->kv_full[0], 0, guard));
-      if (ok) {
+    // the one lane that issues each tcgen05.mma / commit. Across items, Q K^T of an item's first
+    // KV tile follows P V of the previous item's last one for the same Q tile: MMAs of one thread
+    // run in issue order, so it cannot overwrite P before P V reads it. P V with accumulate = 0
+    // overwrites O only after the softmax warpgroup has published the new item's first P, which
+    // it does after reading the previous item's O.
+    constexpr int kFmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
+    constexpr uint32_t kIdescQK = umma_idesc_f16(kFmt, kBM, kBN, 0);
+    constexpr uint32_t kIdescPV = umma_idesc_f16(kFmt, kBM, D, 1);
+    const uint32_t q_addr = smem_u32(q_smem);
+    const uint32_t ring_addr = smem_u32(ring);
+    int consumed = 0;                 // ring index of the item's K_0
+    int q_waits[kQTiles] = {};
+    int p_waits[kQTiles] = {};
+    bool ok = true;
+    bool issued_any = false;
+    auto wait_ring = [&](int i) {
+      return __all_sync(0xffffffffu, mbar_wait(&sb->kv_full[i % kSlots], (i / kSlots) & 1, guard));
+    };
+    auto issue_qk = [&](int t, uint32_t k_addr) {
 #pragma unroll
-        for (int t = 0; t < kQTiles; ++t) {
-          if (n_kv_tile[t] == 0) continue;
-          ok = __all_sync(0xffffffffu, mbar_wait(&sb->q_full[t], 0, guard));
-          if (!ok) break;
-          tc_fence_after();
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            umma_ss_elect(tmem + t * 128, kmajor_desc(q_addr + t * kTileBytes, kk),
-                          kmajor_desc(ring_addr, kk), kIdescQK, kk > 0);
-          }
-          umma_commit_elect(&sb->s_full[t]);
-        }
-        if (ok) umma_commit_elect(&sb->kv_empty[0]);
+      for (int kk = 0; kk < D / 16; ++kk) {
+        umma_ss_elect(tmem + t * 128, kmajor_desc(q_addr + t * kTileBytes, kk),
+                      kmajor_desc(k_addr, kk), kIdescQK, kk > 0);
       }
+      umma_commit_elect(&sb->s_full[t]);
+    };
+    Item it;
+    for (int k = 0; ok && item_at<kPersistent>(a, k, it); ++k) {
+      if (it.qb < 0) continue;
+      int n_kv_tile[kQTiles];
+#pragma unroll
+      for (int t = 0; t < kQTiles; ++t) n_kv_tile[t] = kv_tiles_for(a, it.qb, t);
+      const int n_kv = n_kv_tile[kQTiles - 1];
+      if (n_kv == 0) continue;
+      issued_any = true;
+      const int kbase = consumed;     // K_j at kbase + 2j, V_j at kbase + 2j + 1
+      ok = wait_ring(kbase);
+      if (!ok) break;
+#pragma unroll
+      for (int t = 0; t < kQTiles; ++t) {
+        if (n_kv_tile[t] == 0) continue;
+        ok = __all_sync(0xffffffffu, mbar_wait(&sb->q_full[t], q_waits[t] & 1, guard));
+        if (!ok) break;
+        ++q_waits[t];
+        tc_fence_after();
+        issue_qk(t, ring_addr + (kbase % kSlots) * kTileBytes);
+        if (kPersistent && n_kv_tile[t] == 1) umma_commit_elect(&sb->q_free[t]);   // last Q K^T
+      }
+      if (!ok) break;
+      umma_commit_elect(&sb->kv_empty[kbase % kSlots]);
       for (int j = 0; j < n_kv && ok; ++j) {
-        const int iv = 2 * j + 1;  // V_j ring index
+        const int iv = kbase + 2 * j + 1;  // V_j ring index
         const int sv = iv % kSlots;
-        const int ik = 2 * j + 2;  // K_{j+1} ring index
+        const int ik = iv + 1;             // K_{j+1} ring index
         const int sk = ik % kSlots;
-        ok = __all_sync(0xffffffffu, mbar_wait(&sb->kv_full[sv], (iv / kSlots) & 1, guard));
+        ok = wait_ring(iv);
         if (!ok) break;
         const uint32_t v_addr = ring_addr + sv * kTileBytes;
         const uint32_t k_addr = ring_addr + sk * kTileBytes;
@@ -337,7 +420,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // the softmax warpgroup has stored it.
 #pragma unroll
             for (int ch = 0; ch < kPChunks; ++ch) {
-              ok = __all_sync(0xffffffffu, mbar_wait(&sb->p_half[t][ch], j & 1, guard));
+              ok = __all_sync(0xffffffffu, mbar_wait(&sb->p_half[t][ch], p_waits[t] & 1, guard));
               if (!ok) break;
               tc_fence_after();
 #pragma unroll
@@ -348,30 +431,32 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
             if (!ok) break;
+            ++p_waits[t];
           }
           // V_j is released once the last tile that uses it (always tile 1, whose range is the
-          // CTA's) has its PV issued; K_{j+1} once tile 1's S for it is issued.
+          // item's) has its PV issued; K_{j+1} once tile 1's S for it is issued.
           if (t == kQTiles - 1) umma_commit_elect(&sb->kv_empty[sv]);
           if (j + 1 < n_kv_tile[t]) {
             if (!k_ready) {
-              ok = __all_sync(0xffffffffu, mbar_wait(&sb->kv_full[sk], (ik / kSlots) & 1, guard));
+              ok = wait_ring(ik);
               if (!ok) break;
               tc_fence_after();
               k_ready = true;
             }
-#pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-              umma_ss_elect(tmem + t * 128, kmajor_desc(q_addr + t * kTileBytes, kk),
-                            kmajor_desc(k_addr, kk), kIdescQK, kk > 0);
+            issue_qk(t, k_addr);
+            if (kPersistent && j + 2 == n_kv_tile[t]) {
+              umma_commit_elect(&sb->q_free[t]);   // its last Q K^T
             }
-            umma_commit_elect(&sb->s_full[t]);
           } else if (j + 1 == n_kv_tile[t]) {
             umma_commit_elect(&sb->o_full[t]);
           }
           if (t == kQTiles - 1 && j + 1 < n_kv) umma_commit_elect(&sb->kv_empty[sk]);
         }
       }
-      // Every MMA issued has completed before TMEM may be released.
+      consumed = kbase + 2 * n_kv;
+    }
+    // Every MMA issued has completed before TMEM may be released.
+    if (issued_any) {
       umma_commit_elect(&sb->mma_done);
       mbar_wait(&sb->mma_done, 0, guard);
     }
@@ -380,135 +465,178 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int t = warp >> 2;                  // Q tile of this warpgroup
     const int quarter = warp & 3;             // TMEM lane quarter this warp may access
     const int row_in_tile = quarter * 32 + lane;
-    const int row = q0 + t * kBM + row_in_tile;
     const uint32_t lane_field = static_cast<uint32_t>(quarter * 32) << 16;
     const uint32_t taddr_s = tmem + t * 128 + lane_field;
     const uint32_t taddr_o = tmem + 256 + t * 128 + lane_field;
     const float sl2 = a.scale_log2;
-    const int tile_row0 = q0 + t * kBM;       // first row of this Q tile
-
-    float m_ref = -INFINITY;  // log2-domain reference point of this row
-    float l_sum = 0.f;
+    int s_waits = 0, o_waits = 0;
     bool ok = true;
-    const int n_kv_t = n_kv_tile[t];
-    for (int j = 0; j < n_kv_t; ++j) {
-      if (!mbar_wait(&sb->s_full[t], j & 1, guard)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t s[128];
-      tmem_ld32(taddr_s + 0, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
-      tmem_ld32(taddr_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
-      tmem_ld32(taddr_s + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
-      tmem_ld32(taddr_s + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
-      tmem_ld_wait();
-      float* sf = reinterpret_cast<float*>(s);
+    Item it;
+    for (int k = 0; ok && item_at<kPersistent>(a, k, it); ++k) {
+      if (it.qb < 0) continue;
+      const int b = it.bh / a.heads, h = it.bh - b * a.heads;
+      const int tile_row0 = it.qb * kRowsPerCta + t * kBM;   // first row of this Q tile
+      const int row = tile_row0 + row_in_tile;
+      const int n_kv_t = kv_tiles_for(a, it.qb, t);
 
-      const int k0 = j * kBN;
-      const bool tile_needs_mask =
-          (k0 + kBN > a.seqlen_k) || (a.causal && k0 + kBN - 1 > tile_row0 + a.causal_offset);
-      if (tile_needs_mask) {
-        const int limit = min(a.seqlen_k, a.causal ? row + a.causal_offset + 1 : a.seqlen_k);
-        const int visible = limit - k0;  // keys [k0, k0 + visible) are visible to this row
-#pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          if (c >= visible) sf[c] = -INFINITY;
+      float m_ref = -INFINITY;  // log2-domain reference point of this row
+      float l_sum = 0.f;
+      for (int j = 0; j < n_kv_t; ++j) {
+        if (!mbar_wait(&sb->s_full[t], s_waits & 1, guard)) {
+          ok = false;
+          break;
         }
-      }
-      // Row max: 8 independent chains of 3-input maxima over columns 16..127, seeded by 0..15.
-      float mx8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mx8[i] = fmaxf(sf[i], sf[i + 8]);
-#pragma unroll
-      for (int c = 16; c < 128; c += 16) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) mx8[i] = fmax3(mx8[i], sf[c + 2 * i], sf[c + 2 * i + 1]);
-      }
-      const float mx = fmaxf(fmax3(mx8[0], mx8[1], mx8[2]),
-                             fmaxf(fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
-      const float mt = mx == -INFINITY ? -INFINITY : mx * sl2;
+        ++s_waits;
+        tc_fence_after();
+        uint32_t s[128];
+        tmem_ld32(taddr_s + 0, *reinterpret_cast<uint32_t(*)[32]>(&s[0]));
+        tmem_ld32(taddr_s + 32, *reinterpret_cast<uint32_t(*)[32]>(&s[32]));
+        tmem_ld32(taddr_s + 64, *reinterpret_cast<uint32_t(*)[32]>(&s[64]));
+        tmem_ld32(taddr_s + 96, *reinterpret_cast<uint32_t(*)[32]>(&s[96]));
+        tmem_ld_wait();
+        float* sf = reinterpret_cast<float*>(s);
 
-      float m_new = m_ref;
-      if (m_ref == -INFINITY || mt > m_ref + kRescaleThreshold) m_new = fmaxf(m_ref, mt);
-      const bool rescale = (m_new != m_ref) && (m_ref != -INFINITY);
-      const float factor = rescale ? ex2(m_ref - m_new) : 1.f;
-      if (rescale) l_sum *= factor;
-      m_ref = m_new;
-      const float ref = m_ref == -INFINITY ? 0.f : m_ref;
-      if (__any_sync(0xffffffffu, rescale)) {
-        // Rare: the reference point moved by more than the threshold. O holds PV through tile
-        // j-1 (its completion is covered by s_full) and PV of tile j waits for the first P half,
-        // so O is rescaled in place here, 16 columns at a time to keep registers for the scores.
-#pragma unroll 1
-        for (int c = 0; c < D / 16; ++c) {
-          uint32_t ov[16];
-          tmem_ld16(taddr_o + c * 16, ov);
-          tmem_ld_wait();
+        const int k0 = j * kBN;
+        const bool tile_needs_mask =
+            (k0 + kBN > a.seqlen_k) || (a.causal && k0 + kBN - 1 > tile_row0 + a.causal_offset);
+        if (tile_needs_mask) {
+          const int limit = min(a.seqlen_k, a.causal ? row + a.causal_offset + 1 : a.seqlen_k);
+          const int visible = limit - k0;  // keys [k0, k0 + visible) are visible to this row
 #pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            ov[e] = __float_as_uint(__uint_as_float(ov[e]) * factor);
+          for (int c = 0; c < 128; ++c) {
+            if (c >= visible) sf[c] = -INFINITY;
           }
-          tmem_st16(taddr_o + c * 16, ov);
         }
-      }
-
-      // x = s * scale_log2 - ref on pairs; 2^x on the SFU for most pairs and, in tiles without
-      // masked scores, with the FMA-pipe polynomial for kPolyPairs of every 8 pairs (the choice
-      // is made once per tile so the unrolled loop has no branches). P is published to the MMA
-      // warp in kPChunks chunks as soon as each chunk is in TMEM.
-      float ps[4] = {0.f, 0.f, 0.f, 0.f};
-      const float nref = -ref;
-      if (tile_needs_mask) {
-        softmax_exp_store<T, 0, kPChunks>(sf, sl2, nref, ps, taddr_s, sb->p_half[t]);
-      } else {
-        softmax_exp_store<T, kPolyPairs, kPChunks>(sf, sl2, nref, ps, taddr_s, sb->p_half[t]);
-      }
-      l_sum += (ps[0] + ps[1]) + (ps[2] + ps[3]);
-    }
-
-    // Epilogue: O / l in the input dtype, staged in this Q tile's shared-memory buffer (free:
-    // o_full follows every MMA of the tile, its Q K^T included) in the Q tile's swizzled layout,
-    // then written by TMA stores, which clip rows past S_q; and the natural-log LSE.
-    if (ok && n_kv_t > 0) ok = mbar_wait(&sb->o_full[t], 0, guard);
-    uint8_t* stage = q_smem + t * kTileBytes;
-    if (ok) {
-      tc_fence_after();
-      const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+        // Row max: 8 independent chains of 3-input maxima over columns 16..127, seeded by 0..15.
+        float mx8[8];
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t ov[32];
-        if (n_kv_t > 0) {
-          tmem_ld32(taddr_o + c * 32, ov);
-          tmem_ld_wait();
+        for (int i = 0; i < 8; ++i) mx8[i] = fmaxf(sf[i], sf[i + 8]);
+#pragma unroll
+        for (int c = 16; c < 128; c += 16) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) mx8[i] = fmax3(mx8[i], sf[c + 2 * i], sf[c + 2 * i + 1]);
+        }
+        const float mx = fmaxf(fmax3(mx8[0], mx8[1], mx8[2]),
+                               fmaxf(fmax3(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+        const float mt = mx == -INFINITY ? -INFINITY : mx * sl2;
+
+        float m_new = m_ref;
+        if (m_ref == -INFINITY || mt > m_ref + kRescaleThreshold) m_new = fmaxf(m_ref, mt);
+        const bool rescale = (m_new != m_ref) && (m_ref != -INFINITY);
+        const float factor = rescale ? ex2(m_ref - m_new) : 1.f;
+        if (rescale) l_sum *= factor;
+        m_ref = m_new;
+        const float ref = m_ref == -INFINITY ? 0.f : m_ref;
+        if (__any_sync(0xffffffffu, rescale)) {
+          // Rare: the reference point moved by more than the threshold. O holds PV through tile
+          // j-1 (its completion is covered by s_full) and PV of tile j waits for the first P
+          // half, so O is rescaled in place here, 16 columns at a time.
+#pragma unroll 1
+          for (int c = 0; c < D / 16; ++c) {
+            uint32_t ov[16];
+            tmem_ld16(taddr_o + c * 16, ov);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              ov[e] = __float_as_uint(__uint_as_float(ov[e]) * factor);
+            }
+            tmem_st16(taddr_o + c * 16, ov);
+          }
+        }
+
+        // x = s * scale_log2 - ref on pairs; 2^x on the SFU for most pairs and, in tiles without
+        // masked scores, with the FMA-pipe polynomial for kPolyPairs of every 8 pairs (the
+        // choice is made once per tile so the unrolled loop has no branches). P is published to
+        // the MMA warp in kPChunks chunks as soon as each chunk is in TMEM.
+        float ps[4] = {0.f, 0.f, 0.f, 0.f};
+        const float nref = -ref;
+        if (tile_needs_mask) {
+          softmax_exp_store<T, 0, kPChunks>(sf, sl2, nref, ps, taddr_s, sb->p_half[t]);
         } else {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) ov[e] = 0u;
+          softmax_exp_store<T, kPolyPairs, kPChunks>(sf, sl2, nref, ps, taddr_s, sb->p_half[t]);
         }
-        const float* of = reinterpret_cast<const float*>(ov);
+        l_sum += (ps[0] + ps[1]) + (ps[2] + ps[3]);
+      }
+
+      // Epilogue: O / l in the input dtype, and the natural-log LSE. Reading O (tcgen05.ld +
+      // wait) happens before this warpgroup publishes the next item's first P, which the next
+      // item's first P V (accumulate = 0) waits for.
+      if (ok && n_kv_t > 0) {
+        ok = mbar_wait(&sb->o_full[t], o_waits & 1, guard);
+        ++o_waits;
+      }
+      if (kPersistent && !ok) break;   // (the one-item form must reach its barrier below)
+      tc_fence_after();
+      const bool row_ok = row < a.seqlen_q;
+      const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+      if constexpr (kPersistent) {
+        // One 2 D-byte row per thread (the Q buffers already hold the next item's Q).
+        T* orow = static_cast<T*>(a.o) + static_cast<int64_t>(b) * a.o_batch_stride +
+                  static_cast<int64_t>(row) * a.o_seq_stride +
+                  static_cast<int64_t>(h) * a.o_head_stride;
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          const int chunk = c * 4 + v;      // 16-byte chunk of the row: 8 per 64-column box
-          *reinterpret_cast<uint4*>(stage + (chunk >> 3) * kBoxBytes + sw128_offset(
-              static_cast<uint32_t>(row_in_tile), static_cast<uint32_t>(chunk & 7))) =
-              pack8<T>(of + 8 * v, inv);
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t ov[32];
+          if (n_kv_t > 0) {
+            tmem_ld32(taddr_o + c * 32, ov);
+            tmem_ld_wait();
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) ov[e] = 0u;
+          }
+          if (row_ok) {
+            const float* of = reinterpret_cast<const float*>(ov);
+            uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) dst[v] = pack8<T>(of + 8 * v, inv);
+          }
+        }
+      } else {
+        // Staged in this Q tile's buffer (free: o_full follows every MMA of the tile, its Q K^T
+        // included; a Q tile without keys was never loaded) in the Q tile's swizzled layout,
+        // then written by TMA stores, which clip rows past S_q.
+        // Every thread of the warpgroup reaches the barrier, whatever its waits returned.
+        uint8_t* stage = q_smem + t * kTileBytes;
+        if (ok) {
+#pragma unroll
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t ov[32];
+            if (n_kv_t > 0) {
+              tmem_ld32(taddr_o + c * 32, ov);
+              tmem_ld_wait();
+            } else {
+#pragma unroll
+              for (int e = 0; e < 32; ++e) ov[e] = 0u;
+            }
+            const float* of = reinterpret_cast<const float*>(ov);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              const int chunk = c * 4 + v;    // 16-byte chunk of the row: 8 per 64-column box
+              *reinterpret_cast<uint4*>(stage + (chunk >> 3) * kBoxBytes + sw128_offset(
+                  static_cast<uint32_t>(row_in_tile), static_cast<uint32_t>(chunk & 7))) =
+                  pack8<T>(of + 8 * v, inv);
+            }
+          }
+          fence_proxy_async_shared();
+        }
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + t) : "memory");   // this warpgroup only
+        if (threadIdx.x % 128 == 0 && ok && !sb->abort_flag) {
+#pragma unroll
+          for (int box = 0; box < D / 64; ++box) {
+            tma_store_4d(&tmo, stage + box * kBoxBytes, box * 64,
+                         tma_c(a.oc, 1, tile_row0, h, b), tma_c(a.oc, 2, tile_row0, h, b),
+                         tma_c(a.oc, 3, tile_row0, h, b));
+          }
+          tma_store_commit();
+          tma_store_wait_read();   // the CTA may exit once the stores have read the stage
         }
       }
-      fence_proxy_async_shared();
-      if (row < a.seqlen_q) {
+      if (!ok) break;
+      if (row_ok) {
         a.lse[(static_cast<int64_t>(b) * a.heads + h) * a.seqlen_q + row] =
             l_sum > 0.f ? m_ref * 0.69314718055994530942f + logf(l_sum) : -INFINITY;
       }
-    }
-    asm volatile("bar.sync %0, 128;" ::"r"(1 + t) : "memory");   // this warpgroup only
-    if (threadIdx.x % 128 == 0 && ok && !sb->abort_flag) {
-#pragma unroll
-      for (int box = 0; box < D / 64; ++box) {
-        tma_store_4d(&tmo, stage + box * kBoxBytes, box * 64, tma_c(a.oc, 1, tile_row0, h, b),
-                     tma_c(a.oc, 2, tile_row0, h, b), tma_c(a.oc, 3, tile_row0, h, b));
-      }
-      tma_store_commit();
-      tma_store_wait_read();   // the CTA may exit once the stores have read the stage
+      tc_fence_before();
     }
   }
 
@@ -520,66 +648,59 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// The four tensor maps of a launch: q, k, v loads and the o store.
+// The tensor maps of a launch: q, k and v loads and the o store (one-item form).
 struct Maps {
   CUtensorMap q, k, v, o;
 };
 
 // One shared-memory opt-in per (kernel instantiation, device) and host thread.
-template <typename T, int D, int kPoly, int kChunks>
+template <typename T, int D, int kPoly, bool kPersistent>
 int launch_variant(const PrefillArgs& a, const Maps& m, int grid, int dev, cudaStream_t stream) {
   constexpr int kSmemBytes = Geometry<D>::kSmemBytes;
+  auto kernel = prefill_kernel<T, D, kPoly, kDefaultPChunks, kPersistent>;
   static thread_local int configured_device = -1;
   if (configured_device != dev) {
-    if (int st = check_cuda(cudaFuncSetAttribute(prefill_kernel<T, D, kPoly, kChunks>,
+    if (int st = check_cuda(cudaFuncSetAttribute(kernel,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  kSmemBytes),
                             "cudaFuncSetAttribute(prefill)"))
       return st;
     configured_device = dev;
   }
-  prefill_kernel<T, D, kPoly, kChunks><<<grid, kThreads, kSmemBytes, stream>>>(a, m.q, m.k, m.v, m.o);
+  kernel<<<grid, kThreads, kSmemBytes, stream>>>(a, m.q, m.k, m.v, m.o);
   return check_cuda(cudaGetLastError(), "prefill_kernel launch");
 }
 
-// Tuning knobs read once per process: FLASH_LAB_PREFILL_POLY_PAIRS=0|2|3|4 (pairs of every 8
-// whose 2^x runs on the FMA pipe) and FLASH_LAB_PREFILL_P_CHUNKS=1|2 (chunks P is published in).
-int env_choice(const char* name, int fallback, int a, int b, int c, int d) {
-  const char* env = std::getenv(name);
-  if (env == nullptr) return fallback;
-  const int v = std::atoi(env);
-  return (v == a || v == b || v == c || v == d) ? v : fallback;
-}
-
+// Tuning knob read once per process: FLASH_LAB_PREFILL_POLY_PAIRS=0|2|3|4, the pairs of every 8
+// whose 2^x runs on the FMA pipe (head_dim 128; head_dim 64 runs the default).
 int poly_pairs() {
-  static const int value = env_choice("FLASH_LAB_PREFILL_POLY_PAIRS", kDefaultPolyPairs, 0, 2, 3, 4);
+  static const int value = [] {
+    const char* env = std::getenv("FLASH_LAB_PREFILL_POLY_PAIRS");
+    if (env == nullptr) return kDefaultPolyPairs;
+    const int v = std::atoi(env);
+    return (v == 0 || v == 2 || v == 3 || v == 4) ? v : kDefaultPolyPairs;
+  }();
   return value;
 }
 
-int p_chunks() {
-  static const int value = env_choice("FLASH_LAB_PREFILL_P_CHUNKS", kDefaultPChunks, 1, 2, 1, 2);
-  return value;
-}
-
-template <typename T, int kChunks>
-int launch_poly(const PrefillArgs& a, const Maps& m, int grid, int dev, cudaStream_t stream) {
-  switch (poly_pairs()) {
-    case 0: return launch_variant<T, 128, 0, kChunks>(a, m, grid, dev, stream);
-    case 2: return launch_variant<T, 128, 2, kChunks>(a, m, grid, dev, stream);
-    case 3: return launch_variant<T, 128, 3, kChunks>(a, m, grid, dev, stream);
-    default: return launch_variant<T, 128, 4, kChunks>(a, m, grid, dev, stream);
-  }
-}
-
-// head_dim 128 takes the tuning knobs; head_dim 64 runs the default variant.
+// head_dim 128: one item per CTA (measured faster there); head_dim 64: persistent CTAs.
 template <typename T>
-int launch_prefill(const PrefillArgs& a, const Maps& m, int head_dim, int grid, int dev, cudaStream_t stream) {
+int launch_prefill(const PrefillArgs& a, const Maps& m, int head_dim, int sm_count, int dev,
+                   cudaStream_t stream) {
+  const int64_t items = static_cast<int64_t>(a.batch) * a.heads * a.q_blocks;
   if (head_dim == 64) {
-    return launch_variant<T, 64, kDefaultPolyPairs, kDefaultPChunks>(a, m, grid, dev,
-                                                                     stream);
+    const int64_t units =
+        static_cast<int64_t>(a.batch) * a.heads * (a.causal ? (a.q_blocks + 1) / 2 : a.q_blocks);
+    const int grid = static_cast<int>(std::min<int64_t>(units, sm_count));
+    return launch_variant<T, 64, kDefaultPolyPairs, true>(a, m, grid, dev, stream);
   }
-  if (p_chunks() == 1) return launch_poly<T, 1>(a, m, grid, dev, stream);
-  return launch_poly<T, 2>(a, m, grid, dev, stream);
+  const int grid = static_cast<int>(items);
+  switch (poly_pairs()) {
+    case 0: return launch_variant<T, 128, 0, false>(a, m, grid, dev, stream);
+    case 2: return launch_variant<T, 128, 2, false>(a, m, grid, dev, stream);
+    case 3: return launch_variant<T, 128, 3, false>(a, m, grid, dev, stream);
+    default: return launch_variant<T, 128, 4, false>(a, m, grid, dev, stream);
+  }
 }
 
 int validate(const flb_attn_params* p) {
@@ -635,11 +756,11 @@ extern "C" int flb_prefill_fwd(const flb_attn_params* p, flb_stream_t stream_) {
     return fail(FLB_ERR_MISALIGNED, "k must have 16-byte aligned rows (data pointer and strides)");
   if (!rows_16b_aligned(vv))
     return fail(FLB_ERR_MISALIGNED, "v must have 16-byte aligned rows (data pointer and strides)");
-  View4 ov{p->o, {p->batch, p->seqlen_q, p->heads, p->head_dim},
-           {p->o_batch_stride, p->o_seq_stride, p->o_head_stride, 1}, 2};
   if (int st = encode_rows_x64_map(&m.q, &a.qc, qv, kBM, p->dtype)) return st;
   if (int st = encode_rows_x64_map(&m.k, &a.kc, kv, kBN, p->dtype)) return st;
   if (int st = encode_rows_x64_map(&m.v, &a.vc, vv, kBN, p->dtype)) return st;
+  View4 ov{p->o, {p->batch, p->seqlen_q, p->heads, p->head_dim},
+           {p->o_batch_stride, p->o_seq_stride, p->o_head_stride, 1}, 2};
   if (int st = encode_rows_x64_map(&m.o, &a.oc, ov, kBM, p->dtype)) return st;
 
   a.o = p->o;
@@ -660,9 +781,8 @@ extern "C" int flb_prefill_fwd(const flb_attn_params* p, flb_stream_t stream_) {
   a.scale = p->softmax_scale;
   a.scale_log2 = static_cast<float>(static_cast<double>(p->softmax_scale) * 1.4426950408889634);
 
-  const int grid = a.q_blocks * p->batch * p->heads;
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   if (p->dtype == FLB_BF16)
-    return launch_prefill<__nv_bfloat16>(a, m, p->head_dim, grid, dev, stream);
-  return launch_prefill<__half>(a, m, p->head_dim, grid, dev, stream);
+    return launch_prefill<__nv_bfloat16>(a, m, p->head_dim, sm_count, dev, stream);
+  return launch_prefill<__half>(a, m, p->head_dim, sm_count, dev, stream);
 }

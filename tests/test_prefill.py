@@ -41,6 +41,8 @@ SHAPES_D64 = [
     (2, 37, 101, 4, 2, 64),
     (1, 101, 37, 4, 4, 64),
     (1, 600, 129, 2, 1, 64),
+    # more work units than SMs, so persistent CTAs run several items; causal rows < 700 see no keys
+    (2, 1000, 300, 64, 8, 64),
 ]
 
 
