@@ -70,6 +70,7 @@ struct DecodeArgs {
   int split_offset;       // index of this launch's first split in the partial arrays
   int splits_total;       // split dimension of the partial arrays
   int key_begin, key_end; // absolute key window of this launch
+  int len_offset;         // seq_lens count keys from this key on (a shard's first key)
   int write_partials;     // 0: write o / lse (num_splits must be 1); 1: write partials
   float scale_log2;
   TmaCoords kc, vc;
@@ -291,7 +292,7 @@ __global__ void __launch_bounds__(kDecodeThreads)
 
   // This split's key range: the window clamped to the sequence length, cut into num_splits
   // ranges that are whole numbers of tiles (the last one shorter).
-  int len = a.seq_lens[b];
+  int len = a.seq_lens[b] - a.len_offset;
   len = min(max(len, 0), a.max_seqlen);
   const int lo = max(a.key_begin, 0);
   const int hi = min(a.key_end, len);
@@ -539,7 +540,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
   const int head0 = hkv * a.group + chunk * kF32MaxHeads;
   const int heads_here = min(kF32MaxHeads, a.group - chunk * kF32MaxHeads);
 
-  int len = a.seq_lens[b];
+  int len = a.seq_lens[b] - a.len_offset;
   len = min(max(len, 0), a.max_seqlen);
   const int lo = max(a.key_begin, 0);
   const int hi = min(a.key_end, len);
@@ -1083,8 +1084,8 @@ extern "C" int flb_decode_fwd(const flb_decode_params* p, flb_stream_t stream_) 
 }
 
 extern "C" int flb_decode_partials(const flb_decode_params* p, int32_t key_begin,
-                                   int32_t key_end, float* partial_o, float* partial_ml,
-                                   flb_stream_t stream_) {
+                                   int32_t key_end, int32_t seq_offset, float* partial_o,
+                                   float* partial_ml, flb_stream_t stream_) {
   clear_error();
   if (p == nullptr) return fail(FLB_ERR_INVALID_ARGUMENT, "params is NULL");
   flb_decode_params q = *p;
@@ -1110,6 +1111,7 @@ extern "C" int flb_decode_partials(const flb_decode_params* p, int32_t key_begin
   a.vc = vc;
   a.key_begin = key_begin;
   a.key_end = key_end;
+  a.len_offset = seq_offset;
   a.num_splits = q.num_splits;
   a.split_offset = 0;
   a.splits_total = q.num_splits;
@@ -1187,8 +1189,9 @@ extern "C" size_t flb_peer_exchange_bytes(int32_t world, int32_t batch, int32_t 
 }
 
 extern "C" int flb_decode_partials_push(const flb_decode_params* p, int32_t key_begin,
-                                        int32_t key_end, const flb_peer_exchange* x,
-                                        int32_t parity, flb_stream_t stream_) {
+                                        int32_t key_end, int32_t seq_offset,
+                                        const flb_peer_exchange* x, int32_t parity,
+                                        flb_stream_t stream_) {
   clear_error();
   if (p == nullptr) return fail(FLB_ERR_INVALID_ARGUMENT, "params is NULL");
   if (int st = check_exchange(x)) return st;
@@ -1214,6 +1217,7 @@ extern "C" int flb_decode_partials_push(const flb_decode_params* p, int32_t key_
   a.vc = vc;
   a.key_begin = key_begin;
   a.key_end = key_end;
+  a.len_offset = seq_offset;
   a.num_splits = q.num_splits;
   a.split_offset = x->rank * q.num_splits;
   a.splits_total = x->world * q.num_splits;

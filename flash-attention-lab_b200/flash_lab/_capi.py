@@ -82,7 +82,7 @@ SIGNATURES = {
     "flb_decode_num_splits": ([_i32, _i32, _i32, _i32, _i32, _i32], ctypes.c_int),
     "flb_decode_workspace_bytes": ([_i32, _i32, _i32, _i32], ctypes.c_size_t),
     "flb_decode_fwd": ([ctypes.POINTER(DecodeParams), _p], ctypes.c_int),
-    "flb_decode_partials": ([ctypes.POINTER(DecodeParams), _i32, _i32, _p, _p, _p],
+    "flb_decode_partials": ([ctypes.POINTER(DecodeParams), _i32, _i32, _i32, _p, _p, _p],
                             ctypes.c_int),
     "flb_decode_merge": ([_p, _p, _i32, _i32, _i32, _i32, _i32, _p, _i64, _i64, _p, _p],
                          ctypes.c_int),
@@ -95,7 +95,7 @@ SIGNATURES = {
     "flb_peer_close": ([_p], ctypes.c_int),
     "flb_peer_free": ([_p], ctypes.c_int),
     "flb_peer_exchange_bytes": ([_i32, _i32, _i32, _i32, _i32], ctypes.c_size_t),
-    "flb_decode_partials_push": ([ctypes.POINTER(DecodeParams), _i32, _i32,
+    "flb_decode_partials_push": ([ctypes.POINTER(DecodeParams), _i32, _i32, _i32,
                                   ctypes.POINTER(PeerExchange), _i32, _p], ctypes.c_int),
     "flb_decode_merge_peers": ([ctypes.POINTER(PeerExchange), _i32, ctypes.c_uint64, _i32, _i32,
                                 _i32, _i32, _i32, _p, _i64, _i64, _p, _p, _p], ctypes.c_int),

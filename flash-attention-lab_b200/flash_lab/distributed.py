@@ -6,8 +6,9 @@ phases:
 
   1. partials: every rank runs the split-KV decode kernel over its shard
      (flb_decode_partials). It writes fp32 (m, l, O) partials for `splits_per_rank` key ranges
-     of each (sequence, head). The shard's valid length, clamp(seq_lens - offset, 0, S_shard), is
-     computed on the device, so nothing is read back to the host.
+     of each (sequence, head). The kernel takes the global seq_lens and the shard's first key
+     and clamps each length to the shard on the device (clamp(seq_lens - offset, 0, S_shard)),
+     so nothing is read back to the host and no extra kernel runs.
   2. exchange: an all_gather over the process group (NCCL over NVLink) gives every rank the
      partials of all ranks, in rank order.
   3. merge: flb_decode_merge combines the N * splits_per_rank partials of each (b, h) in that
@@ -59,7 +60,8 @@ class ShardSpec:
 
 
 def local_lengths(seq_lens: torch.Tensor, shard: ShardSpec) -> torch.Tensor:
-    """Valid keys of each sequence inside the shard, computed on the device (no host sync)."""
+    """Valid keys of each sequence inside the shard (on the device, no host sync). The kernels
+    apply the same clamp themselves; this is for callers and tests."""
     return (seq_lens - shard.offset).clamp_(0, shard.length).to(torch.int32).contiguous()
 
 
@@ -74,14 +76,15 @@ def _dtype_code(dtype: torch.dtype) -> int:
 
 
 def shard_partials(q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.Tensor,
-                   local_lens: torch.Tensor, splits: int, softmax_scale: float):
-    """Phase 1 on this rank: partials [B, H, splits, D] and (m, l) [B, H, splits, 2], fp32."""
+                   seq_lens: torch.Tensor, seq_offset: int, splits: int, softmax_scale: float):
+    """Phase 1 on this rank: partials [B, H, splits, D] and (m, l) [B, H, splits, 2], fp32.
+    seq_lens are the global lengths; the shard holds keys from seq_offset on."""
     lib = _capi.load()
     batch, heads, head_dim = q.shape
     po = torch.empty((batch, heads, splits, head_dim), device=q.device, dtype=torch.float32)
     pml = torch.empty((batch, heads, splits, 2), device=q.device, dtype=torch.float32)
     p = _capi.DecodeParams(
-        q.data_ptr(), k_shard.data_ptr(), v_shard.data_ptr(), 0, 0, local_lens.data_ptr(),
+        q.data_ptr(), k_shard.data_ptr(), v_shard.data_ptr(), 0, 0, seq_lens.data_ptr(),
         q.stride(0), q.stride(1),
         k_shard.stride(0), k_shard.stride(1), k_shard.stride(2),
         v_shard.stride(0), v_shard.stride(1), v_shard.stride(2),
@@ -89,8 +92,9 @@ def shard_partials(q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.Tensor
         batch, heads, k_shard.shape[2], head_dim, k_shard.shape[1], splits, _dtype_code(q.dtype),
         float(softmax_scale), 0, 0, 0,
     )
-    rc = lib.flb_decode_partials(ctypes.byref(p), 0, k_shard.shape[1], po.data_ptr(),
-                                 pml.data_ptr(), torch.cuda.current_stream(q.device).cuda_stream)
+    rc = lib.flb_decode_partials(ctypes.byref(p), 0, k_shard.shape[1], int(seq_offset),
+                                 po.data_ptr(), pml.data_ptr(),
+                                 torch.cuda.current_stream(q.device).cuda_stream)
     if rc != _capi.FLB_OK:
         raise RuntimeError(f"flb_decode_partials: {_capi.error_message(lib, rc)}")
     return po, pml
@@ -201,7 +205,8 @@ class PeerExchange:
         self._opened = []
 
 
-def _decode_sharded_peer(q3, k_shard, v_shard, lens, splits, scale, exchange: PeerExchange):
+def _decode_sharded_peer(q3, k_shard, v_shard, seq_lens, seq_offset, splits, scale,
+                         exchange: PeerExchange):
     lib = exchange._lib
     batch, heads, head_dim = q3.shape
     if exchange.shape != (batch, heads, head_dim, splits):
@@ -209,7 +214,7 @@ def _decode_sharded_peer(q3, k_shard, v_shard, lens, splits, scale, exchange: Pe
                          f"{exchange.shape}, got {(batch, heads, head_dim, splits)}")
     stream = torch.cuda.current_stream(q3.device).cuda_stream
     p = _capi.DecodeParams(
-        q3.data_ptr(), k_shard.data_ptr(), v_shard.data_ptr(), 0, 0, lens.data_ptr(),
+        q3.data_ptr(), k_shard.data_ptr(), v_shard.data_ptr(), 0, 0, seq_lens.data_ptr(),
         q3.stride(0), q3.stride(1),
         k_shard.stride(0), k_shard.stride(1), k_shard.stride(2),
         v_shard.stride(0), v_shard.stride(1), v_shard.stride(2),
@@ -218,7 +223,7 @@ def _decode_sharded_peer(q3, k_shard, v_shard, lens, splits, scale, exchange: Pe
         float(scale), 0, 0, exchange.status.data_ptr(),
     )
     parity = exchange.steps & 1
-    rc = lib.flb_decode_partials_push(ctypes.byref(p), 0, k_shard.shape[1],
+    rc = lib.flb_decode_partials_push(ctypes.byref(p), 0, k_shard.shape[1], int(seq_offset),
                                       ctypes.byref(exchange.x), parity, stream)
     if rc != _capi.FLB_OK:
         raise RuntimeError(f"flb_decode_partials_push: {_capi.error_message(lib, rc)}")
@@ -256,14 +261,15 @@ def decode_sharded(q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.Tensor
                          f"{shard.length}")
     q3 = q[:, 0] if q.dim() == 4 else q
     scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(q3.shape[-1])
-    lens = local_lengths(seq_lens, shard)
+    if seq_lens.dtype != torch.int32 or not seq_lens.is_contiguous():
+        raise ValueError("seq_lens must be contiguous int32")
     if exchange is not None:
-        o, lse = _decode_sharded_peer(q3, k_shard, v_shard, lens, splits_per_rank, scale,
-                                      exchange)
+        o, lse = _decode_sharded_peer(q3, k_shard, v_shard, seq_lens, shard.offset,
+                                      splits_per_rank, scale, exchange)
         if q.dim() == 4:
             o = o.unsqueeze(1)
         return (o, lse) if return_lse else o
-    po, pml = _partials(q3, k_shard, v_shard, lens, splits_per_rank, scale)
+    po, pml = _partials(q3, k_shard, v_shard, seq_lens, shard.offset, splits_per_rank, scale)
     if dist.is_initialized() and dist.get_world_size(group) > 1:
         po, pml = gather_in_rank_order(po, pml, group)
     o, lse = _merge(po, pml, q3.dtype)

@@ -171,14 +171,18 @@ size_t flb_decode_static_scratch_bytes(void);
 /*
  * Raw split partials for a cross-GPU merge: runs the decode kernel on this device's keys
  * [key_begin, key_end) of every sequence (clamped to its length), cut into `num_splits` ranges
- * of the same rounding as flb_decode_fwd, and writes
+ * of the same rounding as flb_decode_fwd. The cache holds a sequence's keys from key seq_offset
+ * on (0 for a whole cache; a shard's first key otherwise), and seq_lens count keys from key 0,
+ * so a sequence's length in this cache is clamp(seq_lens[b] - seq_offset, 0, max_seqlen). It
+ * writes
  *   partial_o  [B, H, num_splits, D] fp32  unnormalised sum_j 2^(s_j - m) v_j
  *   partial_ml [B, H, num_splits, 2] fp32  (m, l), m the log2-domain reference (-inf if empty)
  * No counterpart in the reference (single GPU); it generalises the split stage of
  * csrc/decode/decode.cu:41-202.
  */
 int flb_decode_partials(const flb_decode_params* params, int32_t key_begin, int32_t key_end,
-                        float* partial_o, float* partial_ml, flb_stream_t stream);
+                        int32_t seq_offset, float* partial_o, float* partial_ml,
+                        flb_stream_t stream);
 
 /*
  * Fixed-order log-sum-exp merge of `num_splits` partials per (b, h) laid out as above (the
@@ -226,14 +230,15 @@ size_t flb_peer_exchange_bytes(int32_t world, int32_t batch, int32_t heads, int3
                                int32_t splits_per_rank);
 
 /*
- * This rank's split stage (flb_decode_partials on keys [key_begin, key_end) with
+ * This rank's split stage (flb_decode_partials on keys [key_begin, key_end), seq_offset, with
  * params->num_splits splits) writing its partials at global split indices
  * [rank * S, rank * S + S) of parity region `parity` in EVERY rank's buffer. Once all its CTAs
  * have written, the launch adds 1, with release semantics at system scope, to counter [rank] of
  * every buffer: after n pushes every counter a rank waits on reads n.
  */
 int flb_decode_partials_push(const flb_decode_params* params, int32_t key_begin,
-                             int32_t key_end, const flb_peer_exchange* exchange, int32_t parity,
+                             int32_t key_end, int32_t seq_offset,
+                             const flb_peer_exchange* exchange, int32_t parity,
                              flb_stream_t stream);
 
 /*

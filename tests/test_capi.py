@@ -111,7 +111,7 @@ def test_peer_exchange_host_validation(lib):
     p = _capi.DecodeParams()
     x = _capi.PeerExchange()
     x.world, x.rank = 2, 0           # buffers left NULL
-    assert lib.flb_decode_partials_push(ctypes.byref(p), 0, 1, ctypes.byref(x), 0, None) \
+    assert lib.flb_decode_partials_push(ctypes.byref(p), 0, 1, 0, ctypes.byref(x), 0, None) \
         == _capi.FLB_ERR_INVALID_ARGUMENT
     assert b"buffer of rank 0" in lib.flb_last_error()
     x.world = 9

@@ -28,8 +28,9 @@ from flash_lab.distributed import ShardSpec, decode_sharded, local_lengths, merg
 TILE = 64  # keys per decode tile: split ranges are whole numbers of tiles
 
 
-def numpy_partials(q3, k_shard, v_shard, lens, splits, scale):
+def numpy_partials(q3, k_shard, v_shard, seq_lens, seq_offset, splits, scale):
     """Reference partials with the kernel's split boundaries (fp64 on the CPU)."""
+    lens = (seq_lens - seq_offset).clamp(0, k_shard.shape[1])
     q = q3.double().numpy()
     k = k_shard.double().numpy()
     v = v_shard.double().numpy()
@@ -133,7 +134,7 @@ def _window_partials(q3, kc, vc, lens, key_begin, key_end, splits, scale):
         vc.stride(0), vc.stride(1), vc.stride(2), 0, 0,
         batch, heads, kc.shape[2], head_dim, kc.shape[1], splits, _capi.FLB_BF16, scale, 0, 0,
         0)
-    rc = lib.flb_decode_partials(ctypes.byref(p), key_begin, key_end, po.data_ptr(),
+    rc = lib.flb_decode_partials(ctypes.byref(p), key_begin, key_end, 0, po.data_ptr(),
                                  pml.data_ptr(), torch.cuda.current_stream().cuda_stream)
     assert rc == 0, _capi.error_message(lib, rc)
     return po, pml
@@ -156,7 +157,7 @@ def test_emulated_shards_are_bitwise_equal_to_global_windows(world, splits):
         shard = ShardSpec.even(smax, world, r)
         ks = kc[:, shard.offset:shard.offset + shard.length].contiguous()
         vs = vc[:, shard.offset:shard.offset + shard.length].contiguous()
-        po, pml = shard_partials(q, ks, vs, local_lengths(lens, shard), splits, scale)
+        po, pml = shard_partials(q, ks, vs, lens, shard.offset, splits, scale)
         shard_po.append(po)
         shard_pml.append(pml)
         po, pml = _window_partials(q, kc, vc, lens, shard.offset, shard.offset + shard.length,
