@@ -188,32 +188,11 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
                : "memory");
 }
 
-// Warpgroup-wide register reallocation (all four warps of the warpgroup execute it).
-template <int kRegs>
-__device__ __forceinline__ void warpgroup_regs_inc() {
-  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegs));
-}
-template <int kRegs>
-__device__ __forceinline__ void warpgroup_regs_dec() {
-  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegs));
-}
-
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-// True on exactly one (the elected) lane of the calling warp; all lanes must call it.
-__device__ __forceinline__ bool elect_one_lane() {
-  uint32_t pred = 0;
-  asm volatile(
-      "{\n\t.reg .pred e;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "selp.b32 %0, 1, 0, e;\n\t}"
-      : "=r"(pred));
-  return pred != 0;
 }
 
 // Shared-memory matrix descriptor (sm100 layout): start address, leading/stride byte offsets,
