@@ -41,6 +41,10 @@ constexpr int kDecodeThreads = (kDecodeConsumerWarps + 1) * 32;
 constexpr int kMaxHeadsPerCta = 16;                 // M of the warp MMA
 constexpr int kMaxSplits = 256;
 constexpr int kMaxDest = FLB_MAX_PEERS;             // destinations of pushed partials
+constexpr int kMaxBalancedBatch = 128;              // sequences a length-balanced launch takes
+constexpr int kDecodeBarBytes = 256;                // mbarriers and the abort flag
+// Length-balanced launches keep the chunk prefix sums [batch + 1] and lengths [batch] here.
+constexpr int kDecodeAuxBytes = ((2 * kMaxBalancedBatch + 1) * 4 + 127) / 128 * 128;
 
 struct DecodeArgs {
   const void* q;
@@ -72,6 +76,10 @@ struct DecodeArgs {
   int key_begin, key_end; // absolute key window of this launch
   int len_offset;         // seq_lens count keys from this key on (a shard's first key)
   int write_partials;     // 0: write o / lse (num_splits must be 1); 1: write partials
+  // 1: length-balanced key ranges (balanced_prefix), 16-bit kernel of flb_decode_fwd only; the
+  // cross-warp merge then has its own shared-memory area of merge_rows rows per warp.
+  int balanced;
+  int merge_rows;
   float scale_log2;
   TmaCoords kc, vc;
 };
@@ -87,7 +95,14 @@ struct DecodeCfg {
       kDecodeConsumerWarps * kMaxHeadsPerCta * (D + 2) * 4;
   static constexpr int kRingBytes = kStages * kStageBytes;
   static constexpr int kDataBytes = kRingBytes > kMergeBytes ? kRingBytes : kMergeBytes;
-  static constexpr int kSmemBytes = kDataBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kAuxOffset = kDataBytes + kDecodeBarBytes;
+  static constexpr int kMergeOffset = kAuxOffset + kDecodeAuxBytes;   // balanced launches
+  // Dynamic shared memory of a launch: the ring (where a uniform launch also merges its warps),
+  // barriers, the balanced prefix sums, 1024 bytes of alignment slack, and for a balanced launch
+  // a merge area of merge_bytes(merge_rows).
+  static constexpr int kSmemBytes = kMergeOffset + 1024;
+  static constexpr int merge_bytes(int rows) { return kDecodeConsumerWarps * rows * (D + 2) * 4; }
+  static_assert(kMergeBytes <= kRingBytes, "a uniform launch merges its warps in the ring");
 };
 
 __device__ __forceinline__ int tma_c(const TmaCoords& c, int slot, int s, int h, int b) {
@@ -102,15 +117,17 @@ __device__ __forceinline__ int tma_c(const TmaCoords& c, int slot, int s, int h,
 // the warp holds two windows of 32 entries (lane i: pages base + i and base + 32 + i), loading
 // the next window one window ahead, and each lane takes its box's entry by shuffle. Keys past
 // the split's end are still loaded (zeros or other blocks' rows) and masked by the consumers.
+// The ring position continues from t_base tiles (earlier segments of the same CTA); returns the
+// ring position after the tiles it issued.
 template <int kTileKeys, int kColBoxes, int kColsPerBox, int kColBoxBytes, int kRowBytes,
           int kStages, int kTileBytes>
-__device__ __forceinline__ void produce_kv(const DecodeArgs& a, const CUtensorMap* tmk,
-                                           const CUtensorMap* tmv, uint8_t* ring,
-                                           uint64_t* full_bar, uint64_t* empty_bar, int k0,
-                                           int ntiles, int hkv, int b, const WaitGuard& guard,
-                                           int lane) {
+__device__ __forceinline__ int produce_kv(const DecodeArgs& a, const CUtensorMap* tmk,
+                                          const CUtensorMap* tmv, uint8_t* ring,
+                                          uint64_t* full_bar, uint64_t* empty_bar, int k0,
+                                          int ntiles, int hkv, int b, int t_base,
+                                          const WaitGuard& guard, int lane) {
   constexpr int kStageBytes = 2 * kTileBytes;
-  if (ntiles <= 0) return;
+  if (ntiles <= 0) return t_base;
   if (lane == 0) {
     tma_prefetch_desc(tmk);
     tma_prefetch_desc(tmv);
@@ -133,11 +150,12 @@ __device__ __forceinline__ void produce_kv(const DecodeArgs& a, const CUtensorMa
     cur = p0 < a.max_blocks ? __ldg(a.block_tables + bt_row + p0) : -1;
     next = p1 < a.max_blocks ? __ldg(a.block_tables + bt_row + p1) : -1;
   }
-  int issued = 0;
+  int issued = t_base;
   for (int t = 0; t < ntiles; ++t) {
-    const int s = t % kStages;
+    const int r = t_base + t;   // ring position
+    const int s = r % kStages;
     bool ok = true;
-    if (t >= kStages) ok = mbar_wait(&empty_bar[s], ((t / kStages) - 1) & 1, guard);
+    if (r >= kStages) ok = mbar_wait(&empty_bar[s], ((r / kStages) - 1) & 1, guard);
     if (!__all_sync(0xffffffffu, ok)) break;
     uint8_t* dst = ring + s * kStageBytes + kind * kTileBytes;
     const int key = k0 + t * kTileKeys + j * box_rows;
@@ -164,14 +182,90 @@ __device__ __forceinline__ void produce_kv(const DecodeArgs& a, const CUtensorMa
                   cb * kColsPerBox, tma_c(crd, 1, row, hkv, blk), tma_c(crd, 2, row, hkv, blk),
                   tma_c(crd, 3, row, hkv, blk));
     }
-    issued = t + 1;
+    issued = r + 1;
   }
-  // Do not leave the CTA while copies are still landing in shared memory.
+  return issued;
+}
+
+// The producer's last step: do not leave the CTA while copies are still landing in shared
+// memory (the last kStages of the `issued` ring positions).
+template <int kStages>
+__device__ __forceinline__ void drain_kv(uint64_t* full_bar, int issued, const WaitGuard& guard,
+                                         int lane) {
   if (lane == 0) {
     for (int t = issued > kStages ? issued - kStages : 0; t < issued; ++t) {
       if (!mbar_wait(&full_bar[t % kStages], (t / kStages) & 1, guard)) break;
     }
   }
+}
+
+// Length-balanced partition of a launch's keys (16-bit kernel of flb_decode_fwd). Sequence b
+// holds n_b = ceil(L_b / 64) chunks of 64 keys, L_b its length clamped to [0, S_max]. The
+// T = batch * num_splits CTAs of one (KV head, head chunk) column share the concatenated chunk
+// list evenly: CTA c takes chunks [floor(c N / T), floor((c + 1) N / T)), N = sum of n_b, which
+// may hold the end of one sequence and the start of the next. A CTA writes one partial per
+// sequence it touches, in slot h (batch + T) + b + c of query head h, so the merge of (b, h)
+// reads the slots of the CTAs from the one holding b's first chunk to the one holding its last.
+// With equal lengths every CTA holds one sequence's 1/num_splits, as in a uniform launch.
+//
+// One warp writes pref[0..batch] (exclusive prefix sums of n_b) and lens[0..batch).
+__device__ __forceinline__ void balanced_prefix(const int* seq_lens, int batch, int len_offset,
+                                                int max_seqlen, int* pref, int* lens, int lane) {
+  constexpr int kPerLane = kMaxBalancedBatch / 32;
+  int n[kPerLane];
+  int sum = 0;
+#pragma unroll
+  for (int j = 0; j < kPerLane; ++j) {
+    const int b = lane * kPerLane + j;
+    int len = 0;
+    if (b < batch) {
+      len = min(max(seq_lens[b] - len_offset, 0), max_seqlen);
+      lens[b] = len;
+    }
+    n[j] = (len + kDecodeBK - 1) / kDecodeBK;
+    sum += n[j];
+  }
+  int incl = sum;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += v;
+  }
+  int run = incl - sum;
+#pragma unroll
+  for (int j = 0; j < kPerLane; ++j) {
+    const int b = lane * kPerLane + j;
+    if (b < batch) pref[b] = run;
+    run += n[j];
+  }
+  if (lane == 31) pref[batch] = incl;
+}
+
+// The sequence that holds chunk x (x < N): the largest b < batch with pref[b] <= x (sequences
+// without chunks share their start with the next one). For x >= N, batch - 1.
+__device__ __forceinline__ int sequence_of_chunk(const int* pref, int batch, int64_t x) {
+  int lo = 0, hi = batch - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (pref[mid] <= x) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
+
+// True on every one of the 128 consumer threads when pred holds on any of them (named barrier
+// 1 with an OR reduction), so that all of them take the same branch after it.
+__device__ __forceinline__ bool consumers_any(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "n"(kDecodeConsumerWarps * 32)
+      : "memory");
+  return r != 0;
 }
 
 // Publishes a push once per launch (called by one thread per CTA after the CTA's partial stores,
@@ -205,29 +299,30 @@ __device__ __forceinline__ void store_out(T* p, float v) {
   }
 }
 
-// The end of a split CTA, shared by the 16-bit and the fp32 kernels: the consumer warps have
-// left their per-warp (m, l, O) in shared memory (wm, wl [warps][16], wo [warps][16][D]). Merges
-// the warps in a fixed order and writes either o / lse (one split) or this split's partials to
-// every destination, then publishes a push. Called by the 128 consumer threads.
+// The end of a split CTA's segment, shared by the 16-bit and the fp32 kernels: the consumer
+// warps have left their per-warp (m, l, O) in shared memory (wm, wl [warps][mrows],
+// wo [warps][mrows][D]). Merges the warps in a fixed order and writes either o / lse (one split)
+// or the segment's partials to every destination (query head h in slot seg_slot + h h_stride),
+// then publishes a push. Called by the 128 consumer threads.
 template <typename T, int D>
 __device__ __forceinline__ void finish_split(const DecodeArgs& a, const float* wm, const float* wl,
                                              const float* wo, int heads_here, int head0, int b,
-                                             int split) {
+                                             int64_t seg_slot, int64_t h_stride, int mrows) {
   const int tid = threadIdx.x;
   for (int idx = tid; idx < heads_here * D; idx += kDecodeConsumerWarps * 32) {
     const int row = idx / D;
     const int d = idx - row * D;
     float m = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kDecodeConsumerWarps; ++w) m = fmaxf(m, wm[w * kMaxHeadsPerCta + row]);
+    for (int w = 0; w < kDecodeConsumerWarps; ++w) m = fmaxf(m, wm[w * mrows + row]);
     float num = 0.f, den = 0.f;
 #pragma unroll
     for (int w = 0; w < kDecodeConsumerWarps; ++w) {
-      const float mw = wm[w * kMaxHeadsPerCta + row];
+      const float mw = wm[w * mrows + row];
       if (mw != -INFINITY) {
         const float f = ex2(mw - m);
-        num += wo[(w * kMaxHeadsPerCta + row) * D + d] * f;
-        den += wl[w * kMaxHeadsPerCta + row] * f;
+        num += wo[(w * mrows + row) * D + d] * f;
+        den += wl[w * mrows + row] * f;
       }
     }
     const int h = head0 + row;
@@ -240,8 +335,7 @@ __device__ __forceinline__ void finish_split(const DecodeArgs& a, const float* w
             den > 0.f ? m * 0.69314718055994530942f + logf(den) : -INFINITY;
       }
     } else {
-      const int64_t slot =
-          (static_cast<int64_t>(b) * a.heads + h) * a.splits_total + a.split_offset + split;
+      const int64_t slot = seg_slot + h * h_stride;
       for (int dst = 0; dst < a.n_dest; ++dst) {
         a.partial_o[dst][slot * D + d] = num;
         if (d == 0) {
@@ -277,6 +371,8 @@ __global__ void __launch_bounds__(kDecodeThreads)
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + Cfg::kDataBytes);
   uint64_t* empty_bar = full_bar + kStages;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(empty_bar + kStages);
+  int* pref = reinterpret_cast<int*>(smem + Cfg::kAuxOffset);   // [batch + 1], balanced only
+  int* lens = pref + kMaxBalancedBatch + 1;                       // [batch], balanced only
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -290,21 +386,22 @@ __global__ void __launch_bounds__(kDecodeThreads)
   const int head0 = hkv * a.group + chunk * kMaxHeadsPerCta;
   const int heads_here = min(kMaxHeadsPerCta, a.group - chunk * kMaxHeadsPerCta);
 
-  // This split's key range: the window clamped to the sequence length, cut into num_splits
-  // ranges that are whole numbers of tiles (the last one shorter).
-  int len = a.seq_lens[b] - a.len_offset;
-  len = min(max(len, 0), a.max_seqlen);
-  const int lo = max(a.key_begin, 0);
-  const int hi = min(a.key_end, len);
-  const int n = hi - lo;
-  int k0 = 0, k1 = 0;
-  if (n > 0) {
-    const int per = (n + a.num_splits - 1) / a.num_splits;
-    const int per_split = (per + kDecodeBK - 1) / kDecodeBK * kDecodeBK;
-    k0 = lo + split * per_split;
-    k1 = min(hi, k0 + per_split);
+  // Uniform launch: this split's key range, the window clamped to the sequence length and cut
+  // into num_splits ranges that are whole numbers of tiles (the last one shorter).
+  int k0u = 0, k1u = 0;
+  if (!a.balanced) {
+    int len = a.seq_lens[b] - a.len_offset;
+    len = min(max(len, 0), a.max_seqlen);
+    const int lo = max(a.key_begin, 0);
+    const int hi = min(a.key_end, len);
+    const int n = hi - lo;
+    if (n > 0) {
+      const int per = (n + a.num_splits - 1) / a.num_splits;
+      const int per_split = (per + kDecodeBK - 1) / kDecodeBK * kDecodeBK;
+      k0u = lo + split * per_split;
+      k1u = min(hi, k0u + per_split);
+    }
   }
-  const int ntiles = k1 > k0 ? (k1 - k0 + kDecodeBK - 1) / kDecodeBK : 0;
 
   if (threadIdx.x == 0) {
     *abort_flag = 0;
@@ -314,180 +411,247 @@ __global__ void __launch_bounds__(kDecodeThreads)
     }
     fence_barrier_init();
   }
+  if (a.balanced && warp == kDecodeConsumerWarps)
+    balanced_prefix(a.seq_lens, a.batch, a.len_offset, a.max_seqlen, pref, lens, lane);
   __syncthreads();
   const WaitGuard guard{abort_flag, a.status};
 
+  // Segments of this CTA: one per sequence it touches, sequences [sb_begin, sb_end) at most.
+  // Uniform: sequence b only (its split may be empty and still writes its partial).
+  const int total = a.batch * a.num_splits;   // CTAs per column (balanced)
+  const int c = b * a.num_splits + split;     // this CTA's place in its column
+  int64_t g0 = 0, g1 = 0;
+  int sb_begin = b, sb_end = b + 1;
+  if (a.balanced) {
+    const int64_t n = pref[a.batch];
+    g0 = static_cast<int64_t>(c) * n / total;
+    g1 = static_cast<int64_t>(c + 1) * n / total;
+    sb_begin = sequence_of_chunk(pref, a.batch, g0);
+    sb_end = a.batch;
+  }
+  // Key range [k0, k1) of this CTA's part of sequence sb: 1 = run it, 0 = nothing of sb here,
+  // -1 = no later sequence either.
+  auto segment = [&](int sb, int& k0, int& k1) -> int {
+    if (!a.balanced) {
+      k0 = k0u;
+      k1 = k1u;
+      return 1;
+    }
+    if (pref[sb] >= g1) return -1;
+    const int64_t lo = max(g0, static_cast<int64_t>(pref[sb]));
+    const int64_t hi = min(g1, static_cast<int64_t>(pref[sb + 1]));
+    if (lo >= hi) return 0;
+    k0 = static_cast<int>(lo - pref[sb]) * kDecodeBK;
+    k1 = min(static_cast<int>(hi - pref[sb]) * kDecodeBK, lens[sb]);
+    return 1;
+  };
+
   if (warp == kDecodeConsumerWarps) {
     // ---------------- producer warp ----------------
-    produce_kv<kDecodeBK, Cfg::kBoxes, 64, Cfg::kBoxBytes, 128, kStages, Cfg::kTileBytes>(
-        a, &tmk, &tmv, smem, full_bar, empty_bar, k0, ntiles, hkv, b, guard, lane);
+    int issued = 0;
+    for (int sb = sb_begin; sb < sb_end; ++sb) {
+      int k0 = 0, k1 = 0;
+      const int st = segment(sb, k0, k1);
+      if (st < 0) break;
+      if (st == 0) continue;
+      const int nt = k1 > k0 ? (k1 - k0 + kDecodeBK - 1) / kDecodeBK : 0;
+      issued = produce_kv<kDecodeBK, Cfg::kBoxes, 64, Cfg::kBoxBytes, 128, kStages,
+                          Cfg::kTileBytes>(a, &tmk, &tmv, smem, full_bar, empty_bar, k0, nt, hkv,
+                                           sb, issued, guard, lane);
+      if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
+    }
+    drain_kv<kStages>(full_bar, issued, guard, lane);
     return;
   }
 
   // ---------------- consumer warps ----------------
   const int g = lane >> 2;   // fragment row group
   const int t4 = lane & 3;   // thread in quad
-
-  // Q as the A operand: rows = query heads of the group (zero beyond heads_here).
-  uint32_t qa[kKSteps][4];
-  {
-    const T* qb = static_cast<const T*>(a.q) + static_cast<int64_t>(b) * a.q_batch_stride;
-    const bool r0 = g < heads_here, r1 = g + 8 < heads_here;
-    const T* q0 = qb + static_cast<int64_t>(head0 + g) * a.q_head_stride;
-    const T* q1 = qb + static_cast<int64_t>(head0 + g + 8) * a.q_head_stride;
-#pragma unroll
-    for (int kk = 0; kk < kKSteps; ++kk) {
-      const int c = kk * 16 + 2 * t4;
-      qa[kk][0] = r0 ? *reinterpret_cast<const uint32_t*>(q0 + c) : 0u;
-      qa[kk][1] = r1 ? *reinterpret_cast<const uint32_t*>(q1 + c) : 0u;
-      qa[kk][2] = r0 ? *reinterpret_cast<const uint32_t*>(q0 + c + 8) : 0u;
-      qa[kk][3] = r1 ? *reinterpret_cast<const uint32_t*>(q1 + c + 8) : 0u;
-    }
-  }
-
-  float o_acc[kNTiles][4];
-#pragma unroll
-  for (int j = 0; j < kNTiles; ++j) o_acc[j][0] = o_acc[j][1] = o_acc[j][2] = o_acc[j][3] = 0.f;
-  float m_run[2] = {-INFINITY, -INFINITY};  // log2-domain running max, rows g and g + 8
-  float l_run[2] = {0.f, 0.f};              // this thread's share of the row sums
-
   const uint32_t smem_base = smem_u32(smem);
   // ldmatrix row addresses (lane-dependent parts), see sw128_offset.
   const uint32_t k_row = static_cast<uint32_t>(warp * 16 + (lane >> 4) * 8 + (lane & 7));
   const uint32_t k_chunk_lo = static_cast<uint32_t>((lane >> 3) & 1);
   const uint32_t v_row = static_cast<uint32_t>(warp * 16 + ((lane >> 3) & 1) * 8 + (lane & 7));
   const uint32_t v_chunk_lo = static_cast<uint32_t>(lane >> 4);
+  // Cross-warp merge area: the ring once a uniform launch has consumed it; its own area in a
+  // balanced launch, whose producer is already loading the next segment.
+  const int mrows = a.merge_rows;
+  float* wm = reinterpret_cast<float*>(smem + (a.balanced ? Cfg::kMergeOffset : 0));  // [warps][mrows]
+  float* wl = wm + kDecodeConsumerWarps * mrows;                                      // [warps][mrows]
+  float* wo = wl + kDecodeConsumerWarps * mrows;                                      // [warps][mrows][D]
 
-  bool ok = true;
-  for (int t = 0; t < ntiles; ++t) {
-    const int s = t % kStages;
-    if (!mbar_wait(&full_bar[s], (t / kStages) & 1, guard)) {
-      ok = false;
-      break;
-    }
-    const uint32_t kbase = smem_base + s * Cfg::kStageBytes;
-    const uint32_t vbase = kbase + Cfg::kTileBytes;
-    const int key_w = k0 + t * kDecodeBK + warp * 16;   // first key of this warp's slice
-    const int valid = k1 - key_w;                       // keys of the slice before the end
+  int t_base = 0;   // ring position of the segment's first tile
+  for (int sb = sb_begin; sb < sb_end; ++sb) {
+    int k0 = 0, k1 = 0;
+    const int st = segment(sb, k0, k1);
+    if (st < 0) break;
+    if (st == 0) continue;
+    const int ntiles = k1 > k0 ? (k1 - k0 + kDecodeBK - 1) / kDecodeBK : 0;
 
-    // S = Q K^T over this warp's 16 keys (two n-tiles of 8 keys).
-    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    // Q as the A operand: rows = query heads of the group (zero beyond heads_here).
+    uint32_t qa[kKSteps][4];
+    {
+      const T* qb = static_cast<const T*>(a.q) + static_cast<int64_t>(sb) * a.q_batch_stride;
+      const bool r0 = g < heads_here, r1 = g + 8 < heads_here;
+      const T* q0 = qb + static_cast<int64_t>(head0 + g) * a.q_head_stride;
+      const T* q1 = qb + static_cast<int64_t>(head0 + g + 8) * a.q_head_stride;
 #pragma unroll
-    for (int kk = 0; kk < kKSteps; ++kk) {
-      const uint32_t chunk = 2 * kk + k_chunk_lo;
-      const uint32_t addr = kbase + (chunk >> 3) * Cfg::kBoxBytes + sw128_offset(k_row, chunk & 7);
-      uint32_t b0, b1, b2, b3;
-      ldsm_x4(addr, b0, b1, b2, b3);
-      mma_16816<T>(sc[0], qa[kk], b0, b1);
-      mma_16816<T>(sc[1], qa[kk], b2, b3);
-    }
-
-    // Online softmax in the exp2 domain; keys at or past k1 are hidden.
-    float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int key = nt * 8 + 2 * t4 + (e & 1);
-        const float v = key < valid ? sc[nt][e] * a.scale_log2 : -INFINITY;
-        sc[nt][e] = v;
-        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      for (int kk = 0; kk < kKSteps; ++kk) {
+        const int col = kk * 16 + 2 * t4;
+        qa[kk][0] = r0 ? *reinterpret_cast<const uint32_t*>(q0 + col) : 0u;
+        qa[kk][1] = r1 ? *reinterpret_cast<const uint32_t*>(q1 + col) : 0u;
+        qa[kk][2] = r0 ? *reinterpret_cast<const uint32_t*>(q0 + col + 8) : 0u;
+        qa[kk][3] = r1 ? *reinterpret_cast<const uint32_t*>(q1 + col + 8) : 0u;
       }
     }
-    float ref[2], resc[2];
+
+    float o_acc[kNTiles][4];
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-      const float m_new = fmaxf(m_run[r], mx[r]);
-      ref[r] = m_new == -INFINITY ? 0.f : m_new;
-      resc[r] = ex2(m_run[r] - ref[r]);
-      m_run[r] = m_new;
+    for (int j = 0; j < kNTiles; ++j) o_acc[j][0] = o_acc[j][1] = o_acc[j][2] = o_acc[j][3] = 0.f;
+    float m_run[2] = {-INFINITY, -INFINITY};  // log2-domain running max, rows g and g + 8
+    float l_run[2] = {0.f, 0.f};              // this thread's share of the row sums
+
+    bool ok = true;
+    for (int t = 0; t < ntiles; ++t) {
+      const int r = t_base + t;
+      const int s = r % kStages;
+      if (!mbar_wait(&full_bar[s], (r / kStages) & 1, guard)) {
+        ok = false;
+        break;
+      }
+      const uint32_t kbase = smem_base + s * Cfg::kStageBytes;
+      const uint32_t vbase = kbase + Cfg::kTileBytes;
+      const int key_w = k0 + t * kDecodeBK + warp * 16;   // first key of this warp's slice
+      const int valid = k1 - key_w;                       // keys of the slice before the end
+
+      // S = Q K^T over this warp's 16 keys (two n-tiles of 8 keys).
+      float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int kk = 0; kk < kKSteps; ++kk) {
+        const uint32_t ch = 2 * kk + k_chunk_lo;
+        const uint32_t addr = kbase + (ch >> 3) * Cfg::kBoxBytes + sw128_offset(k_row, ch & 7);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(addr, b0, b1, b2, b3);
+        mma_16816<T>(sc[0], qa[kk], b0, b1);
+        mma_16816<T>(sc[1], qa[kk], b2, b3);
+      }
+
+      // Online softmax in the exp2 domain; keys at or past k1 are hidden.
+      float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = nt * 8 + 2 * t4 + (e & 1);
+          const float v = key < valid ? sc[nt][e] * a.scale_log2 : -INFINITY;
+          sc[nt][e] = v;
+          mx[e >> 1] = fmaxf(mx[e >> 1], v);
+        }
+      }
+      float ref[2], resc[2];
+#pragma unroll
+      for (int rr = 0; rr < 2; ++rr) {
+        mx[rr] = fmaxf(mx[rr], __shfl_xor_sync(0xffffffffu, mx[rr], 1));
+        mx[rr] = fmaxf(mx[rr], __shfl_xor_sync(0xffffffffu, mx[rr], 2));
+        const float m_new = fmaxf(m_run[rr], mx[rr]);
+        ref[rr] = m_new == -INFINITY ? 0.f : m_new;
+        resc[rr] = ex2(m_run[rr] - ref[rr]);
+        m_run[rr] = m_new;
+      }
+      float p[2][4];
+      float psum[2] = {0.f, 0.f};
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          p[nt][e] = ex2(sc[nt][e] - ref[e >> 1]);
+          psum[e >> 1] += p[nt][e];
+        }
+      }
+      l_run[0] = l_run[0] * resc[0] + psum[0];
+      l_run[1] = l_run[1] * resc[1] + psum[1];
+#pragma unroll
+      for (int j = 0; j < kNTiles; ++j) {
+        o_acc[j][0] *= resc[0];
+        o_acc[j][1] *= resc[0];
+        o_acc[j][2] *= resc[1];
+        o_acc[j][3] *= resc[1];
+      }
+      uint32_t pa[4];
+      pa[0] = pack2<T>(p[0][0], p[0][1]);
+      pa[1] = pack2<T>(p[0][2], p[0][3]);
+      pa[2] = pack2<T>(p[1][0], p[1][1]);
+      pa[3] = pack2<T>(p[1][2], p[1][3]);
+
+      // V rows of hidden keys are masked to zero in the B fragments (0 * NaN would poison O).
+      // Fragment keys: regs 0/2 hold keys 2*t4 + {0,1}, regs 1/3 keys 8 + 2*t4 + {0,1}.
+      uint32_t vmask_lo = 0xffffffffu, vmask_hi = 0xffffffffu;
+      if (valid < 16) {
+        const int kl = 2 * t4, kh = 8 + 2 * t4;
+        vmask_lo = (kl < valid ? 0x0000ffffu : 0u) | (kl + 1 < valid ? 0xffff0000u : 0u);
+        vmask_hi = (kh < valid ? 0x0000ffffu : 0u) | (kh + 1 < valid ? 0xffff0000u : 0u);
+      }
+#pragma unroll
+      for (int jp = 0; jp < kNTiles / 2; ++jp) {
+        const uint32_t ch = 2 * jp + v_chunk_lo;
+        const uint32_t addr = vbase + (ch >> 3) * Cfg::kBoxBytes + sw128_offset(v_row, ch & 7);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_trans(addr, b0, b1, b2, b3);
+        mma_16816<T>(o_acc[2 * jp], pa, b0 & vmask_lo, b1 & vmask_hi);
+        mma_16816<T>(o_acc[2 * jp + 1], pa, b2 & vmask_lo, b3 & vmask_hi);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty_bar[s]);
     }
-    float p[2][4];
-    float psum[2] = {0.f, 0.f};
+    t_base += ntiles;
+
+    // Full row sums of this warp.
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        p[nt][e] = ex2(sc[nt][e] - ref[e >> 1]);
-        psum[e >> 1] += p[nt][e];
+    for (int rr = 0; rr < 2; ++rr) {
+      l_run[rr] += __shfl_xor_sync(0xffffffffu, l_run[rr], 1);
+      l_run[rr] += __shfl_xor_sync(0xffffffffu, l_run[rr], 2);
+    }
+
+    // Every consumer thread is past this segment's tiles and past the previous segment's merge
+    // reads; all of them take the same branch.
+    if (consumers_any(!ok || *abort_flag != 0)) {
+      // A CTA that gave up still counts itself in a push, so the counters stay consistent for
+      // the next step; the status word already tells the host this step's outputs are invalid.
+      if (a.write_partials && a.arrive[0] != nullptr && threadIdx.x == 0) publish_push(a);
+      return;
+    }
+    if (t4 == 0) {
+      if (g < heads_here) {
+        wm[warp * mrows + g] = m_run[0];
+        wl[warp * mrows + g] = l_run[0];
+      }
+      if (g + 8 < heads_here) {
+        wm[warp * mrows + g + 8] = m_run[1];
+        wl[warp * mrows + g + 8] = l_run[1];
       }
     }
-    l_run[0] = l_run[0] * resc[0] + psum[0];
-    l_run[1] = l_run[1] * resc[1] + psum[1];
 #pragma unroll
     for (int j = 0; j < kNTiles; ++j) {
-      o_acc[j][0] *= resc[0];
-      o_acc[j][1] *= resc[0];
-      o_acc[j][2] *= resc[1];
-      o_acc[j][3] *= resc[1];
+      const int col = j * 8 + 2 * t4;
+      if (g < heads_here) {
+        float* r0 = wo + (warp * mrows + g) * D + col;
+        r0[0] = o_acc[j][0];
+        r0[1] = o_acc[j][1];
+      }
+      if (g + 8 < heads_here) {
+        float* r1 = wo + (warp * mrows + g + 8) * D + col;
+        r1[0] = o_acc[j][2];
+        r1[1] = o_acc[j][3];
+      }
     }
-    uint32_t pa[4];
-    pa[0] = pack2<T>(p[0][0], p[0][1]);
-    pa[1] = pack2<T>(p[0][2], p[0][3]);
-    pa[2] = pack2<T>(p[1][0], p[1][1]);
-    pa[3] = pack2<T>(p[1][2], p[1][3]);
+    asm volatile("bar.sync 1, %0;" ::"n"(kDecodeConsumerWarps * 32) : "memory");
 
-    // V rows of hidden keys are masked to zero in the B fragments (0 * NaN would poison O).
-    // Fragment keys: regs 0/2 hold keys 2*t4 + {0,1}, regs 1/3 keys 8 + 2*t4 + {0,1}.
-    uint32_t vmask_lo = 0xffffffffu, vmask_hi = 0xffffffffu;
-    if (valid < 16) {
-      const int kl = 2 * t4, kh = 8 + 2 * t4;
-      vmask_lo = (kl < valid ? 0x0000ffffu : 0u) | (kl + 1 < valid ? 0xffff0000u : 0u);
-      vmask_hi = (kh < valid ? 0x0000ffffu : 0u) | (kh + 1 < valid ? 0xffff0000u : 0u);
-    }
-#pragma unroll
-    for (int jp = 0; jp < kNTiles / 2; ++jp) {
-      const uint32_t chunk = 2 * jp + v_chunk_lo;
-      const uint32_t addr = vbase + (chunk >> 3) * Cfg::kBoxBytes + sw128_offset(v_row, chunk & 7);
-      uint32_t b0, b1, b2, b3;
-      ldsm_x4_trans(addr, b0, b1, b2, b3);
-      mma_16816<T>(o_acc[2 * jp], pa, b0 & vmask_lo, b1 & vmask_hi);
-      mma_16816<T>(o_acc[2 * jp + 1], pa, b2 & vmask_lo, b3 & vmask_hi);
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty_bar[s]);
+    const int64_t seg_slot =
+        a.balanced ? static_cast<int64_t>(sb) + c
+                   : static_cast<int64_t>(b) * a.heads * a.splits_total + a.split_offset + split;
+    const int64_t h_stride = a.balanced ? a.batch + total : a.splits_total;
+    finish_split<T, D>(a, wm, wl, wo, heads_here, head0, sb, seg_slot, h_stride, mrows);
   }
-
-  // Full row sums of this warp.
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 1);
-    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 2);
-  }
-
-  // All consumer warps are past the ring (the producer waited for its last copies), so the ring
-  // memory is reused for the cross-warp merge.
-  asm volatile("bar.sync 1, %0;" ::"n"(kDecodeConsumerWarps * 32) : "memory");
-  if (!ok || *abort_flag) {
-    // A CTA that gave up still counts itself in a push, so the counters stay consistent for the
-    // next step; the status word already tells the host this step's outputs are invalid.
-    if (a.write_partials && a.arrive[0] != nullptr && threadIdx.x == 0) publish_push(a);
-    return;
-  }
-  float* wm = reinterpret_cast<float*>(smem);                         // [warps][16]
-  float* wl = wm + kDecodeConsumerWarps * kMaxHeadsPerCta;            // [warps][16]
-  float* wo = wl + kDecodeConsumerWarps * kMaxHeadsPerCta;            // [warps][16][D]
-  if (t4 == 0) {
-    wm[warp * kMaxHeadsPerCta + g] = m_run[0];
-    wm[warp * kMaxHeadsPerCta + g + 8] = m_run[1];
-    wl[warp * kMaxHeadsPerCta + g] = l_run[0];
-    wl[warp * kMaxHeadsPerCta + g + 8] = l_run[1];
-  }
-#pragma unroll
-  for (int j = 0; j < kNTiles; ++j) {
-    const int col = j * 8 + 2 * t4;
-    float* r0 = wo + (warp * kMaxHeadsPerCta + g) * D + col;
-    float* r1 = wo + (warp * kMaxHeadsPerCta + g + 8) * D + col;
-    r0[0] = o_acc[j][0];
-    r0[1] = o_acc[j][1];
-    r1[0] = o_acc[j][2];
-    r1[1] = o_acc[j][3];
-  }
-  asm volatile("bar.sync 1, %0;" ::"n"(kDecodeConsumerWarps * 32) : "memory");
-
-  finish_split<T, D>(a, wm, wl, wo, heads_here, head0, b, split);
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -567,8 +731,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
 
   if (warp == kDecodeConsumerWarps) {
     // ---------------- producer warp: [32 keys x D] fp32 tiles ----------------
-    produce_kv<kF32BK, 1, D, Cfg::kTileBytes, D * 4, kStages, Cfg::kTileBytes>(
-        a, &tmk, &tmv, smem, full_bar, empty_bar, k0, ntiles, hkv, b, guard, lane);
+    const int issued = produce_kv<kF32BK, 1, D, Cfg::kTileBytes, D * 4, kStages, Cfg::kTileBytes>(
+        a, &tmk, &tmv, smem, full_bar, empty_bar, k0, ntiles, hkv, b, 0, guard, lane);
+    drain_kv<kStages>(full_bar, issued, guard, lane);
     return;
   }
 
@@ -688,8 +853,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
     for (int i = 0; i < kDL; ++i) o[h][i] += __shfl_xor_sync(0xffffffffu, o[h][i], 16);
   }
 
-  asm volatile("bar.sync 1, %0;" ::"n"(kDecodeConsumerWarps * 32) : "memory");
-  if (!ok || *abort_flag) {
+  if (consumers_any(!ok || *abort_flag != 0)) {
     if (a.write_partials && a.arrive[0] != nullptr && threadIdx.x == 0) publish_push(a);
     return;
   }
@@ -713,7 +877,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
   }
   asm volatile("bar.sync 1, %0;" ::"n"(kDecodeConsumerWarps * 32) : "memory");
 
-  finish_split<float, D>(a, wm, wl, wo, heads_here, head0, b, split);
+  finish_split<float, D>(a, wm, wl, wo, heads_here, head0, b,
+                         static_cast<int64_t>(b) * a.heads * a.splits_total + a.split_offset +
+                             split,
+                         a.splits_total, kMaxHeadsPerCta);
 }
 
 // Arrivals a merge waits for: counters[src] >= expected for every source rank (null = none).
@@ -782,6 +949,59 @@ __global__ void decode_merge_kernel(const float* __restrict__ partial_o,
   }
 }
 
+// Merge of a length-balanced launch (balanced_prefix): the same fixed-order log-sum-exp merge as
+// decode_merge_kernel, over the slots of the CTAs that hold a chunk of sequence b, in CTA order.
+// The prefix sums are rebuilt from seq_lens before waiting for the split kernel.
+template <typename T>
+__global__ void decode_merge_balanced_kernel(const float* __restrict__ partial_o,
+                                             const float* __restrict__ partial_ml,
+                                             const int* __restrict__ seq_lens, int batch,
+                                             int heads, int head_dim, int num_splits,
+                                             int max_seqlen, T* o, int64_t o_batch_stride,
+                                             int64_t o_head_stride, float* lse) {
+  __shared__ int pref[kMaxBalancedBatch + 1];
+  __shared__ int lens[kMaxBalancedBatch];
+  if (threadIdx.x < 32) balanced_prefix(seq_lens, batch, 0, max_seqlen, pref, lens, threadIdx.x);
+  __syncthreads();
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int bh = blockIdx.x;
+  const int b = bh / heads;
+  const int h = bh - b * heads;
+  const int total = batch * num_splits;
+  const int64_t n = pref[batch];
+  const int64_t p0 = pref[b], p1 = pref[b + 1];
+  // CTAs holding chunks p0 and p1 - 1: CTA c holds chunk x when c = floor(((x + 1) T - 1) / N).
+  int c_first = 0, c_last = -1;
+  if (p1 > p0) {
+    c_first = static_cast<int>(((p0 + 1) * total - 1) / n);
+    c_last = static_cast<int>((p1 * total - 1) / n);
+  }
+  auto holds = [&](int c) {   // CTA c holds at least one chunk of sequence b
+    const int64_t g0 = static_cast<int64_t>(c) * n / total;
+    const int64_t g1 = static_cast<int64_t>(c + 1) * n / total;
+    return max(g0, p0) < min(g1, p1);
+  };
+  const int64_t base = static_cast<int64_t>(h) * (batch + total) + b;   // + c: CTA c's slot
+  float m = -INFINITY;
+  for (int c = c_first; c <= c_last; ++c)
+    if (holds(c)) m = fmaxf(m, partial_ml[2 * (base + c)]);
+  for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
+    float num = 0.f, den = 0.f;
+    for (int c = c_first; c <= c_last; ++c) {
+      if (!holds(c)) continue;
+      const float ms = partial_ml[2 * (base + c)];
+      if (ms != -INFINITY) {
+        const float f = ex2(ms - m);
+        num += partial_o[(base + c) * head_dim + d] * f;
+        den += partial_ml[2 * (base + c) + 1] * f;
+      }
+    }
+    T* out = o + static_cast<int64_t>(b) * o_batch_stride + static_cast<int64_t>(h) * o_head_stride;
+    store_out<T>(out + d, den > 0.f ? num / den : 0.f);
+    if (d == 0) lse[bh] = den > 0.f ? m * 0.69314718055994530942f + logf(den) : -INFINITY;
+  }
+}
+
 template <typename T, int D>
 int launch_split(const DecodeArgs& args, const CUtensorMap& tmk, const CUtensorMap& tmv,
                  int grid_x, int grid_y, cudaStream_t stream) {
@@ -792,13 +1012,15 @@ int launch_split(const DecodeArgs& args, const CUtensorMap& tmk, const CUtensorM
   if (configured_device != dev) {
     if (int st = check_cuda(cudaFuncSetAttribute(decode_split_kernel<T, D>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 Cfg::kSmemBytes),
+                                                 Cfg::kSmemBytes +
+                                                     Cfg::merge_bytes(kMaxHeadsPerCta)),
                             "cudaFuncSetAttribute(decode)"))
       return st;
     configured_device = dev;
   }
-  decode_split_kernel<T, D><<<dim3(grid_x, grid_y), kDecodeThreads, Cfg::kSmemBytes, stream>>>(
-      args, tmk, tmv);
+  const int smem = Cfg::kSmemBytes + (args.balanced ? Cfg::merge_bytes(args.merge_rows) : 0);
+  decode_split_kernel<T, D><<<dim3(grid_x, grid_y), kDecodeThreads, smem, stream>>>(args, tmk,
+                                                                                   tmv);
   return check_cuda(cudaGetLastError(), "decode_split_kernel launch");
 }
 
@@ -822,6 +1044,34 @@ int launch_merge(const float* po, const float* pml, int batch, int heads, int he
   return check_cuda(cudaLaunchKernelEx(&cfg, decode_merge_kernel<T, kPeers>, po, pml, heads,
                                        head_dim, splits, out, obs, ohs, lse, wait),
                     "decode_merge_kernel launch");
+}
+
+// The merge of a length-balanced launch, for any output dtype (programmatic dependent launch).
+int launch_merge_balanced(const flb_decode_params* p, const float* po, const float* pml,
+                          int splits, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p->batch * p->heads);
+  cfg.blockDim = dim3(p->head_dim);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t err;
+  if (p->dtype == FLB_BF16) {
+    err = cudaLaunchKernelEx(&cfg, decode_merge_balanced_kernel<__nv_bfloat16>, po, pml,
+                             p->seq_lens, p->batch, p->heads, p->head_dim, splits, p->max_seqlen,
+                             static_cast<__nv_bfloat16*>(p->o), p->o_batch_stride,
+                             p->o_head_stride, p->lse);
+  } else {
+    err = cudaLaunchKernelEx(&cfg, decode_merge_balanced_kernel<__half>, po, pml, p->seq_lens,
+                             p->batch, p->heads, p->head_dim, splits, p->max_seqlen,
+                             static_cast<__half*>(p->o), p->o_batch_stride, p->o_head_stride,
+                             p->lse);
+  }
+  return check_cuda(err, "decode_merge_balanced_kernel launch");
 }
 
 int validate(const flb_decode_params* p) {
@@ -934,6 +1184,7 @@ DecodeArgs make_args(const flb_decode_params* p) {
     a.max_blocks = p->max_seqlen / p->page_size;
   }
   a.box_rows = box_rows_for(p);
+  a.merge_rows = kMaxHeadsPerCta;
   return a;
 }
 
@@ -1019,6 +1270,21 @@ int splits_for(int batch, int heads, int heads_kv, int head_dim, int max_seqlen,
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({by_sm, by_len, kMaxSplits})));
 }
 
+// Whether flb_decode_fwd runs p with length-balanced key ranges: more than one split, 16-bit
+// caches, at most kMaxBalancedBatch sequences, and a launch whose extra merge area still lets
+// two CTAs share an SM (as a uniform launch does) or whose grid fits on the SMs at one per SM.
+bool use_balanced(const flb_decode_params* p, int splits, int64_t grid_ctas, int sm_count,
+                  int merge_rows) {
+  if (splits <= 1 || p->dtype == FLB_FP32 || p->batch > kMaxBalancedBatch) return false;
+  const int64_t chunks = (static_cast<int64_t>(p->max_seqlen) + kDecodeBK - 1) / kDecodeBK;
+  if (static_cast<int64_t>(p->batch) * chunks >= (int64_t{1} << 31)) return false;
+  const int smem = p->head_dim == 128
+                       ? DecodeCfg<128>::kSmemBytes + DecodeCfg<128>::merge_bytes(merge_rows)
+                       : DecodeCfg<64>::kSmemBytes + DecodeCfg<64>::merge_bytes(merge_rows);
+  constexpr int kSmemPerSm = 228 * 1024, kReservedPerCta = 1024;
+  return 2 * (smem + kReservedPerCta) <= kSmemPerSm || grid_ctas <= sm_count;
+}
+
 }  // namespace
 }  // namespace flb
 
@@ -1029,10 +1295,21 @@ extern "C" int flb_decode_num_splits(int32_t batch, int32_t heads, int32_t heads
   return splits_for(batch, heads, heads_kv, head_dim, max_seqlen, sm_count);
 }
 
+namespace flb {
+namespace {
+// Partial slots of a flb_decode_fwd workspace: batch * heads * (num_splits + 1), the most a
+// length-balanced launch writes (heads * (batch + batch * num_splits)); a uniform launch uses
+// the first batch * heads * num_splits.
+size_t workspace_slots(int batch, int heads, int num_splits) {
+  return static_cast<size_t>(batch) * heads * (static_cast<size_t>(num_splits) + 1);
+}
+}  // namespace
+}  // namespace flb
+
 extern "C" size_t flb_decode_workspace_bytes(int32_t batch, int32_t heads, int32_t head_dim,
                                              int32_t num_splits) {
   if (num_splits <= 1 || batch <= 0 || heads <= 0 || head_dim <= 0) return 0;
-  const size_t slots = static_cast<size_t>(batch) * heads * num_splits;
+  const size_t slots = workspace_slots(batch, heads, num_splits);
   const size_t o_bytes = (slots * head_dim * sizeof(float) + 255) / 256 * 256;
   return o_bytes + slots * 2 * sizeof(float);
 }
@@ -1070,14 +1347,21 @@ extern "C" int flb_decode_fwd(const flb_decode_params* p, flb_stream_t stream_) 
                 splits, need, p->workspace == nullptr ? size_t(0) : p->workspace_bytes);
   if (reinterpret_cast<uintptr_t>(p->workspace) % 256 != 0)
     return fail(FLB_ERR_MISALIGNED, "workspace must be 256-byte aligned");
-  const size_t slots = static_cast<size_t>(p->batch) * p->heads * splits;
+  const size_t slots = workspace_slots(p->batch, p->heads, splits);
   a.n_dest = 1;
   a.partial_o[0] = static_cast<float*>(p->workspace);
   a.partial_ml[0] = reinterpret_cast<float*>(
       static_cast<char*>(p->workspace) + (slots * p->head_dim * sizeof(float) + 255) / 256 * 256);
   a.write_partials = 1;
+  const int merge_rows = std::min(a.group, kMaxHeadsPerCta);
+  a.balanced = use_balanced(p, splits, static_cast<int64_t>(splits) * grid_y, sm_count,
+                            merge_rows)
+                   ? 1
+                   : 0;
+  if (a.balanced) a.merge_rows = merge_rows;
   if (int st = launch_split_any(p->dtype, p->head_dim, a, tmk, tmv, splits, grid_y, stream))
     return st;
+  if (a.balanced) return launch_merge_balanced(p, a.partial_o[0], a.partial_ml[0], splits, stream);
   return launch_merge_any(p->dtype, a.partial_o[0], a.partial_ml[0], p->batch, p->heads,
                           p->head_dim, splits, p->o, p->o_batch_stride, p->o_head_stride, p->lse,
                           stream);

@@ -8,7 +8,7 @@
 // partials in g_decode_scratch, a file-scope array loaded with this library.
 //
 // Limits and caveats (also in include/flash_lab_b200.h):
-//  * capacity kStaticScratchBytes (8 MiB) per device, enough for B * H * splits <= 16,131
+//  * capacity kStaticScratchBytes (8 MiB) per device, enough for B * H * (splits + 1) <= 16,131
 //    (head_dim 128) or 31,775 (head_dim 64); larger problems get FLB_ERR_WORKSPACE and nothing
 //    runs;
 //  * every GPU that loads the library holds the array until the process exits;

@@ -86,6 +86,11 @@ typedef struct {
  * num_splits: 0 lets the library choose from the shapes only (flb_decode_num_splits), which keeps
  * the call CUDA-graph safe; 1 runs without a merge step. workspace must hold
  * flb_decode_workspace_bytes(...) bytes of device memory when the split count is above 1.
+ * With more than one split, flb_decode_fwd launches batch * num_splits CTAs per KV head. For
+ * 16-bit caches and batch <= 128 their key ranges are length-balanced: the sequences' 64-key
+ * chunks are shared evenly among those CTAs, so a long sequence gets more of them than a short
+ * one (read from seq_lens on the device; still graph safe). Otherwise each sequence is cut into
+ * num_splits equal ranges.
  */
 typedef struct {
   const void* q;
@@ -137,7 +142,8 @@ int flb_prefill_fwd(const flb_attn_params* params, flb_stream_t stream);
 int flb_decode_num_splits(int32_t batch, int32_t heads, int32_t heads_kv, int32_t head_dim,
                           int32_t max_seqlen, int32_t sm_count);
 
-/* Bytes of device workspace flb_decode_fwd needs for this split count (0 when num_splits <= 1).
+/* Bytes of device workspace flb_decode_fwd needs for this split count (0 when num_splits <= 1):
+ * fp32 partials for batch * heads * (num_splits + 1) slots, (head_dim + 2) floats each.
  * Replaces the per-call partial_o / partial_ml allocations (csrc/decode/decode.cu:303-311). */
 size_t flb_decode_workspace_bytes(int32_t batch, int32_t heads, int32_t head_dim,
                                   int32_t num_splits);
@@ -155,8 +161,8 @@ int flb_decode_fwd(const flb_decode_params* params, flb_stream_t stream);
  * flb_decode_fwd computes (the same kernels, the same split count), but keeps the split partials
  * in a static device array of flb_decode_static_scratch_bytes() bytes (8 MiB) instead of a
  * caller workspace; params->workspace is ignored. Problems whose partials do not fit
- * (B * H * splits * (head_dim + 2) * 4 bytes, rounded) return FLB_ERR_WORKSPACE without
- * launching.
+ * (flb_decode_workspace_bytes: B * H * (splits + 1) * (head_dim + 2) * 4 bytes, rounded) return
+ * FLB_ERR_WORKSPACE without launching.
  * Every GPU that loads the library holds the array until exit. All calls on a device share it
  * and it keeps the last call's contents (nothing needs to start at zero), so calls that overlap
  * on the GPU race. The first call on a device looks up the array's address with that device

@@ -86,6 +86,40 @@ def test_split_counts(num_splits, dtype):
     check_decode(out, lse, q, k_cache, v_cache, seq_lens)
 
 
+# Length-balanced key ranges (16-bit caches, more than one split): the sequences' 64-key chunks
+# are shared evenly among batch * num_splits CTAs per KV head, so one CTA may hold the end of one
+# sequence and the start of the next, or several short sequences whole, and some CTAs may hold
+# nothing. Lengths of 0 and past S_max included.
+BALANCED = [
+    # batch, heads, heads_kv, max_seqlen, head_dim, seq_lens, num_splits
+    (8, 32, 8, 4096, 128, [4096, 1, 2, 64, 65, 0, 130, 3000], 2),
+    (8, 8, 8, 1000, 64, [1000, 999, 1, 0, 5000, 63, 64, 65], 3),
+    (5, 16, 2, 3000, 128, [3000, 100, 2900, 50, 1500], 7),    # group 8
+    (3, 32, 2, 2048, 128, [2048, 1, 1024], 4),                  # group 16
+    (2, 64, 2, 700, 128, [700, 699], 5),                         # group 32: two head chunks
+    (4, 8, 4, 200, 64, [1, 2, 3, 4], 16),                        # more CTAs than chunks
+    (12, 32, 4, 8192, 128, "random", 3),
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16],
+                         ids=lambda d: str(d).removeprefix("torch."))
+@pytest.mark.parametrize("case", BALANCED, ids=lambda c: case_id(c) + f"-splits{c[6]}")
+def test_balanced_key_ranges(case, dtype):
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    *shape, splits = case
+    q, k_cache, v_cache, seq_lens = make_case(tuple(shape), dtype, gen)
+    out, lse = flash_lab.decode(q, k_cache, v_cache, seq_lens, impl="splitkv",
+                                num_splits=splits, return_lse=True)
+    again = flash_lab.decode(q, k_cache, v_cache, seq_lens, impl="splitkv", num_splits=splits)
+    assert torch.equal(out, again)
+    lens = seq_lens.clamp(0, k_cache.shape[1])
+    empty = (lens == 0).nonzero().flatten()
+    assert torch.all(out[empty] == 0) and torch.isneginf(lse[empty]).all()
+    keep = (lens > 0).nonzero().flatten()
+    check_decode(out[keep], lse[keep], q[keep], k_cache[keep], v_cache[keep], lens[keep])
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32],
                          ids=lambda d: str(d).removeprefix("torch."))
 @pytest.mark.parametrize("impl", IMPLS)
