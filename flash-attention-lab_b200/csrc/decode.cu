@@ -76,20 +76,24 @@ struct DecodeArgs {
   int key_begin, key_end; // absolute key window of this launch
   int len_offset;         // seq_lens count keys from this key on (a shard's first key)
   int write_partials;     // 0: write o / lse (num_splits must be 1); 1: write partials
-  // 1: length-balanced key ranges (balanced_prefix), 16-bit kernel of flb_decode_fwd only; the
-  // cross-warp merge then has its own shared-memory area of merge_rows rows per warp.
+  // 1: length-balanced key ranges (balanced_prefix), 16-bit kernel of flb_decode_fwd only, over
+  // bal_ctas CTAs per (KV head, head chunk) column; the cross-warp merge then has its own
+  // shared-memory area of merge_rows rows per warp.
   int balanced;
+  int bal_ctas;
   int merge_rows;
   float scale_log2;
   TmaCoords kc, vc;
 };
 
-template <int D>
+// kDeep: the ring of a launch with one CTA per SM, 128 KB instead of 96 KB (measured on B200 with
+// balanced launches: 4 stages of [64 x 128] K and V tiles beat 3 by 2-7 % and 6 stages).
+template <int D, bool kDeep = false>
 struct DecodeCfg {
   static constexpr int kTileBytes = kDecodeBK * D * 2;   // one K or V tile
   static constexpr int kBoxes = D / 64;                  // 64-wide column boxes per tile
   static constexpr int kBoxBytes = kDecodeBK * 128;
-  static constexpr int kStages = D == 128 ? 3 : 6;
+  static constexpr int kStages = kDeep ? (D == 128 ? 4 : 8) : (D == 128 ? 3 : 6);
   static constexpr int kStageBytes = 2 * kTileBytes;
   static constexpr int kMergeBytes =
       kDecodeConsumerWarps * kMaxHeadsPerCta * (D + 2) * 4;
@@ -128,10 +132,6 @@ __device__ __forceinline__ int produce_kv(const DecodeArgs& a, const CUtensorMap
                                           const WaitGuard& guard, int lane) {
   constexpr int kStageBytes = 2 * kTileBytes;
   if (ntiles <= 0) return t_base;
-  if (lane == 0) {
-    tma_prefetch_desc(tmk);
-    tma_prefetch_desc(tmv);
-  }
   const bool paged = a.block_tables != nullptr;
   const int box_rows = paged ? a.box_rows : kTileKeys;
   const int parts = kTileKeys / box_rows;               // boxes along the keys of one tile
@@ -187,6 +187,12 @@ __device__ __forceinline__ int produce_kv(const DecodeArgs& a, const CUtensorMap
   return issued;
 }
 
+// The producer lane's first step, before anything it waits for: fetch both tensor maps.
+__device__ __forceinline__ void prefetch_maps(const CUtensorMap* tmk, const CUtensorMap* tmv) {
+  tma_prefetch_desc(tmk);
+  tma_prefetch_desc(tmv);
+}
+
 // The producer's last step: do not leave the CTA while copies are still landing in shared
 // memory (the last kStages of the `issued` ring positions).
 template <int kStages>
@@ -201,8 +207,7 @@ __device__ __forceinline__ void drain_kv(uint64_t* full_bar, int issued, const W
 
 // Length-balanced partition of a launch's keys (16-bit kernel of flb_decode_fwd). Sequence b
 // holds n_b = ceil(L_b / 64) chunks of 64 keys, L_b its length clamped to [0, S_max]. The
-// T = batch * num_splits CTAs of one (KV head, head chunk) column share the concatenated chunk
-// list evenly: CTA c takes chunks [floor(c N / T), floor((c + 1) N / T)), N = sum of n_b, which
+// T CTAs of one (KV head, head chunk) column share the concatenated chunk list evenly: CTA c takes chunks [floor(c N / T), floor((c + 1) N / T)), N = sum of n_b, which
 // may hold the end of one sequence and the start of the next. A CTA writes one partial per
 // sequence it touches, in slot h (batch + T) + b + c of query head h, so the merge of (b, h)
 // reads the slots of the CTAs from the one holding b's first chunk to the one holding its last.
@@ -352,7 +357,7 @@ __device__ __forceinline__ void finish_split(const DecodeArgs& a, const float* w
 }
 
 
-template <typename T, int D>
+template <typename T, int D, bool kDeep>
 __global__ void __launch_bounds__(kDecodeThreads)
     decode_split_kernel(const __grid_constant__ DecodeArgs a,
                         const __grid_constant__ CUtensorMap tmk,
@@ -360,7 +365,7 @@ __global__ void __launch_bounds__(kDecodeThreads)
   // The merge kernel, launched as a programmatic dependent, may be scheduled once every CTA of
   // this grid has started; it waits (griddepcontrol.wait) for this grid to finish and flush.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-  using Cfg = DecodeCfg<D>;
+  using Cfg = DecodeCfg<D, kDeep>;
   constexpr int kStages = Cfg::kStages;
   constexpr int kKSteps = D / 16;   // MMA k-steps over head_dim
   constexpr int kNTiles = D / 8;    // MMA n-tiles over head_dim in P V
@@ -377,12 +382,15 @@ __global__ void __launch_bounds__(kDecodeThreads)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // Work item: blockIdx.x = split within this launch, blockIdx.y = (b, hkv, head chunk).
-  const int split = blockIdx.x;
+  if (warp == kDecodeConsumerWarps && lane == 0) prefetch_maps(&tmk, &tmv);
+
+  // Work item. Uniform: blockIdx.x = split within this launch, blockIdx.y = (b, hkv, head
+  // chunk). Balanced: blockIdx.x = the CTA's place c in its column, blockIdx.y = (hkv, chunk).
+  const int split = a.balanced ? 0 : blockIdx.x;
   const int chunk = blockIdx.y % a.head_chunks;
   const int bk = blockIdx.y / a.head_chunks;
-  const int hkv = bk % a.heads_kv;
-  const int b = bk / a.heads_kv;
+  const int hkv = a.balanced ? bk : bk % a.heads_kv;
+  const int b = a.balanced ? 0 : bk / a.heads_kv;
   const int head0 = hkv * a.group + chunk * kMaxHeadsPerCta;
   const int heads_here = min(kMaxHeadsPerCta, a.group - chunk * kMaxHeadsPerCta);
 
@@ -418,8 +426,8 @@ __global__ void __launch_bounds__(kDecodeThreads)
 
   // Segments of this CTA: one per sequence it touches, sequences [sb_begin, sb_end) at most.
   // Uniform: sequence b only (its split may be empty and still writes its partial).
-  const int total = a.batch * a.num_splits;   // CTAs per column (balanced)
-  const int c = b * a.num_splits + split;     // this CTA's place in its column
+  const int total = a.bal_ctas;                  // CTAs per column (balanced)
+  const int c = static_cast<int>(blockIdx.x);    // this CTA's place in its column (balanced)
   int64_t g0 = 0, g1 = 0;
   int sb_begin = b, sb_end = b + 1;
   if (a.balanced) {
@@ -696,6 +704,8 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
+  if (warp == kDecodeConsumerWarps && lane == 0) prefetch_maps(&tmk, &tmv);
+
   const int split = blockIdx.x;
   const int chunk = blockIdx.y % a.head_chunks;
   const int bk = blockIdx.y / a.head_chunks;
@@ -956,7 +966,7 @@ template <typename T>
 __global__ void decode_merge_balanced_kernel(const float* __restrict__ partial_o,
                                              const float* __restrict__ partial_ml,
                                              const int* __restrict__ seq_lens, int batch,
-                                             int heads, int head_dim, int num_splits,
+                                             int heads, int head_dim, int total,
                                              int max_seqlen, T* o, int64_t o_batch_stride,
                                              int64_t o_head_stride, float* lse) {
   __shared__ int pref[kMaxBalancedBatch + 1];
@@ -967,7 +977,6 @@ __global__ void decode_merge_balanced_kernel(const float* __restrict__ partial_o
   const int bh = blockIdx.x;
   const int b = bh / heads;
   const int h = bh - b * heads;
-  const int total = batch * num_splits;
   const int64_t n = pref[batch];
   const int64_t p0 = pref[b], p1 = pref[b + 1];
   // CTAs holding chunks p0 and p1 - 1: CTA c holds chunk x when c = floor(((x + 1) T - 1) / N).
@@ -1002,15 +1011,15 @@ __global__ void decode_merge_balanced_kernel(const float* __restrict__ partial_o
   }
 }
 
-template <typename T, int D>
+template <typename T, int D, bool kDeep>
 int launch_split(const DecodeArgs& args, const CUtensorMap& tmk, const CUtensorMap& tmv,
                  int grid_x, int grid_y, cudaStream_t stream) {
-  using Cfg = DecodeCfg<D>;
+  using Cfg = DecodeCfg<D, kDeep>;
   static thread_local int configured_device = -1;  // per-thread cache of the attribute set-up
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_device != dev) {
-    if (int st = check_cuda(cudaFuncSetAttribute(decode_split_kernel<T, D>,
+    if (int st = check_cuda(cudaFuncSetAttribute(decode_split_kernel<T, D, kDeep>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  Cfg::kSmemBytes +
                                                      Cfg::merge_bytes(kMaxHeadsPerCta)),
@@ -1019,8 +1028,8 @@ int launch_split(const DecodeArgs& args, const CUtensorMap& tmk, const CUtensorM
     configured_device = dev;
   }
   const int smem = Cfg::kSmemBytes + (args.balanced ? Cfg::merge_bytes(args.merge_rows) : 0);
-  decode_split_kernel<T, D><<<dim3(grid_x, grid_y), kDecodeThreads, smem, stream>>>(args, tmk,
-                                                                                   tmv);
+  decode_split_kernel<T, D, kDeep><<<dim3(grid_x, grid_y), kDecodeThreads, smem, stream>>>(
+      args, tmk, tmv);
   return check_cuda(cudaGetLastError(), "decode_split_kernel launch");
 }
 
@@ -1048,7 +1057,7 @@ int launch_merge(const float* po, const float* pml, int batch, int heads, int he
 
 // The merge of a length-balanced launch, for any output dtype (programmatic dependent launch).
 int launch_merge_balanced(const flb_decode_params* p, const float* po, const float* pml,
-                          int splits, cudaStream_t stream) {
+                          int ctas, cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p->batch * p->heads);
   cfg.blockDim = dim3(p->head_dim);
@@ -1062,12 +1071,12 @@ int launch_merge_balanced(const flb_decode_params* p, const float* po, const flo
   cudaError_t err;
   if (p->dtype == FLB_BF16) {
     err = cudaLaunchKernelEx(&cfg, decode_merge_balanced_kernel<__nv_bfloat16>, po, pml,
-                             p->seq_lens, p->batch, p->heads, p->head_dim, splits, p->max_seqlen,
+                             p->seq_lens, p->batch, p->heads, p->head_dim, ctas, p->max_seqlen,
                              static_cast<__nv_bfloat16*>(p->o), p->o_batch_stride,
                              p->o_head_stride, p->lse);
   } else {
     err = cudaLaunchKernelEx(&cfg, decode_merge_balanced_kernel<__half>, po, pml, p->seq_lens,
-                             p->batch, p->heads, p->head_dim, splits, p->max_seqlen,
+                             p->batch, p->heads, p->head_dim, ctas, p->max_seqlen,
                              static_cast<__half*>(p->o), p->o_batch_stride, p->o_head_stride,
                              p->lse);
   }
@@ -1218,20 +1227,28 @@ int launch_split_f32_heads(const DecodeArgs& a, const CUtensorMap& tmk, const CU
   return launch_split_f32<D, 1>(a, tmk, tmv, grid_x, grid_y, stream);
 }
 
-// The split kernel for any supported (dtype, head_dim).
+template <typename T, bool kDeep>
+int launch_split_t(int head_dim, const DecodeArgs& a, const CUtensorMap& tmk,
+                   const CUtensorMap& tmv, int grid_x, int grid_y, cudaStream_t stream) {
+  if (head_dim == 128) return launch_split<T, 128, kDeep>(a, tmk, tmv, grid_x, grid_y, stream);
+  return launch_split<T, 64, kDeep>(a, tmk, tmv, grid_x, grid_y, stream);
+}
+
+// The split kernel for any supported (dtype, head_dim); deep: the one-CTA-per-SM ring (16-bit).
 int launch_split_any(int dtype, int head_dim, const DecodeArgs& a, const CUtensorMap& tmk,
-                     const CUtensorMap& tmv, int grid_x, int grid_y, cudaStream_t stream) {
+                     const CUtensorMap& tmv, int grid_x, int grid_y, cudaStream_t stream,
+                     bool deep = false) {
   if (dtype == FLB_FP32) {
     if (head_dim == 128) return launch_split_f32_heads<128>(a, tmk, tmv, grid_x, grid_y, stream);
     return launch_split_f32_heads<64>(a, tmk, tmv, grid_x, grid_y, stream);
   }
   if (dtype == FLB_BF16) {
-    if (head_dim == 128)
-      return launch_split<__nv_bfloat16, 128>(a, tmk, tmv, grid_x, grid_y, stream);
-    return launch_split<__nv_bfloat16, 64>(a, tmk, tmv, grid_x, grid_y, stream);
+    return deep ? launch_split_t<__nv_bfloat16, true>(head_dim, a, tmk, tmv, grid_x, grid_y, stream)
+                : launch_split_t<__nv_bfloat16, false>(head_dim, a, tmk, tmv, grid_x, grid_y,
+                                                       stream);
   }
-  if (head_dim == 128) return launch_split<__half, 128>(a, tmk, tmv, grid_x, grid_y, stream);
-  return launch_split<__half, 64>(a, tmk, tmv, grid_x, grid_y, stream);
+  return deep ? launch_split_t<__half, true>(head_dim, a, tmk, tmv, grid_x, grid_y, stream)
+              : launch_split_t<__half, false>(head_dim, a, tmk, tmv, grid_x, grid_y, stream);
 }
 
 // The merge kernel for any output dtype.
@@ -1270,19 +1287,55 @@ int splits_for(int batch, int heads, int heads_kv, int head_dim, int max_seqlen,
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({by_sm, by_len, kMaxSplits})));
 }
 
-// Whether flb_decode_fwd runs p with length-balanced key ranges: more than one split, 16-bit
-// caches, at most kMaxBalancedBatch sequences, and a launch whose extra merge area still lets
-// two CTAs share an SM (as a uniform launch does) or whose grid fits on the SMs at one per SM.
-bool use_balanced(const flb_decode_params* p, int splits, int64_t grid_ctas, int sm_count,
-                  int merge_rows) {
-  if (splits <= 1 || p->dtype == FLB_FP32 || p->batch > kMaxBalancedBatch) return false;
-  const int64_t chunks = (static_cast<int64_t>(p->max_seqlen) + kDecodeBK - 1) / kDecodeBK;
-  if (static_cast<int64_t>(p->batch) * chunks >= (int64_t{1} << 31)) return false;
-  const int smem = p->head_dim == 128
-                       ? DecodeCfg<128>::kSmemBytes + DecodeCfg<128>::merge_bytes(merge_rows)
-                       : DecodeCfg<64>::kSmemBytes + DecodeCfg<64>::merge_bytes(merge_rows);
+// Dynamic shared memory of a balanced launch of the 16-bit kernel.
+int balanced_smem(int head_dim, bool deep, int merge_rows) {
+  if (head_dim == 128)
+    return deep ? DecodeCfg<128, true>::kSmemBytes + DecodeCfg<128, true>::merge_bytes(merge_rows)
+                : DecodeCfg<128>::kSmemBytes + DecodeCfg<128>::merge_bytes(merge_rows);
+  return deep ? DecodeCfg<64, true>::kSmemBytes + DecodeCfg<64, true>::merge_bytes(merge_rows)
+              : DecodeCfg<64>::kSmemBytes + DecodeCfg<64>::merge_bytes(merge_rows);
+}
+
+bool two_per_sm(int smem) {
   constexpr int kSmemPerSm = 228 * 1024, kReservedPerCta = 1024;
-  return 2 * (smem + kReservedPerCta) <= kSmemPerSm || grid_ctas <= sm_count;
+  return 2 * (smem + kReservedPerCta) <= kSmemPerSm;
+}
+
+// How flb_decode_fwd runs p with more than one split: length-balanced key ranges over `ctas` CTAs
+// per (KV head, head chunk) column (16-bit caches, at most kMaxBalancedBatch sequences), or the
+// uniform split (on = false).
+struct BalancedPlan {
+  bool on = false;
+  bool deep = false;   // the one-CTA-per-SM ring
+  int ctas = 0;
+  int merge_rows = 0;
+};
+
+BalancedPlan plan_balanced(const flb_decode_params* p, int splits, int columns, int group,
+                           int sm_count) {
+  BalancedPlan plan;
+  if (splits <= 1 || p->dtype == FLB_FP32 || p->batch > kMaxBalancedBatch) return plan;
+  const int64_t chunks = (static_cast<int64_t>(p->max_seqlen) + kDecodeBK - 1) / kDecodeBK;
+  if (static_cast<int64_t>(p->batch) * chunks >= (int64_t{1} << 31)) return plan;
+  plan.merge_rows = std::min(group, kMaxHeadsPerCta);
+  const int64_t smem2 = balanced_smem(p->head_dim, false, plan.merge_rows);
+  if (p->num_splits > 0) {
+    // An explicit split count: batch * num_splits CTAs per column with the default ring, while
+    // two of them still fit on an SM or the grid fits on the SMs.
+    plan.ctas = p->batch * splits;
+    plan.on = two_per_sm(smem2) || static_cast<int64_t>(plan.ctas) * columns <= sm_count;
+    return plan;
+  }
+  // Split count left to the library: every SM gets the same number of CTAs. One CTA per SM with
+  // the deep ring, except for caches of small pages (under 64 rows), whose tiles are 8 to 16 TMA
+  // boxes each: there one producer warp per SM cannot issue them fast enough (measured with
+  // 16-row pages: 179 us with one CTA per SM, 157 us with more), so two CTAs share each SM.
+  const bool small_pages = p->block_tables != nullptr && p->page_size < kDecodeBK;
+  const int per_sm = small_pages && two_per_sm(smem2) ? 2 : 1;
+  plan.deep = per_sm == 1;
+  plan.ctas = std::clamp(per_sm * sm_count / columns, p->batch, 2 * p->batch * splits);
+  plan.on = true;
+  return plan;
 }
 
 }  // namespace
@@ -1297,11 +1350,11 @@ extern "C" int flb_decode_num_splits(int32_t batch, int32_t heads, int32_t heads
 
 namespace flb {
 namespace {
-// Partial slots of a flb_decode_fwd workspace: batch * heads * (num_splits + 1), the most a
-// length-balanced launch writes (heads * (batch + batch * num_splits)); a uniform launch uses
-// the first batch * heads * num_splits.
+// Partial slots of a flb_decode_fwd workspace: batch * heads * (2 num_splits + 1), the most a
+// length-balanced launch writes (heads * (batch + T) for T <= 2 batch num_splits CTAs per
+// column); a uniform launch uses the first batch * heads * num_splits.
 size_t workspace_slots(int batch, int heads, int num_splits) {
-  return static_cast<size_t>(batch) * heads * (static_cast<size_t>(num_splits) + 1);
+  return static_cast<size_t>(batch) * heads * (2 * static_cast<size_t>(num_splits) + 1);
 }
 }  // namespace
 }  // namespace flb
@@ -1353,15 +1406,22 @@ extern "C" int flb_decode_fwd(const flb_decode_params* p, flb_stream_t stream_) 
   a.partial_ml[0] = reinterpret_cast<float*>(
       static_cast<char*>(p->workspace) + (slots * p->head_dim * sizeof(float) + 255) / 256 * 256);
   a.write_partials = 1;
-  const int merge_rows = std::min(a.group, kMaxHeadsPerCta);
-  a.balanced = use_balanced(p, splits, static_cast<int64_t>(splits) * grid_y, sm_count,
-                            merge_rows)
-                   ? 1
-                   : 0;
-  if (a.balanced) a.merge_rows = merge_rows;
+  // A balanced launch runs plan.ctas CTAs per (KV head, head chunk) column. With the split
+  // count left to the library every SM gets the same number of CTAs (CTAs that share an SM with
+  // another finish measurably later than CTAs alone).
+  const int columns = p->heads_kv * a.head_chunks;
+  const BalancedPlan plan = plan_balanced(p, splits, columns, a.group, sm_count);
+  if (plan.on) {
+    a.balanced = 1;
+    a.bal_ctas = plan.ctas;
+    a.merge_rows = plan.merge_rows;
+    if (int st = launch_split_any(p->dtype, p->head_dim, a, tmk, tmv, plan.ctas, columns, stream,
+                                  plan.deep))
+      return st;
+    return launch_merge_balanced(p, a.partial_o[0], a.partial_ml[0], plan.ctas, stream);
+  }
   if (int st = launch_split_any(p->dtype, p->head_dim, a, tmk, tmv, splits, grid_y, stream))
     return st;
-  if (a.balanced) return launch_merge_balanced(p, a.partial_o[0], a.partial_ml[0], splits, stream);
   return launch_merge_any(p->dtype, a.partial_o[0], a.partial_ml[0], p->batch, p->heads,
                           p->head_dim, splits, p->o, p->o_batch_stride, p->o_head_stride, p->lse,
                           stream);

@@ -8,7 +8,7 @@
 // partials in g_decode_scratch, a file-scope array loaded with this library.
 //
 // Limits and caveats (also in include/flash_lab_b200.h):
-//  * capacity kStaticScratchBytes (8 MiB) per device, enough for B * H * (splits + 1) <= 16,131
+//  * capacity kStaticScratchBytes (8 MiB) per device, enough for B * H * (2 splits + 1) <= 16,131
 //    (head_dim 128) or 31,775 (head_dim 64); larger problems get FLB_ERR_WORKSPACE and nothing
 //    runs;
 //  * every GPU that loads the library holds the array until the process exits;
@@ -75,8 +75,10 @@ extern "C" int flb_decode_fwd_static(const flb_decode_params* p, flb_stream_t st
                 "flb_decode_fwd_static: B=%d H=%d head_dim=%d with %d splits needs %zu bytes of "
                 "scratch; the static array holds %zu (use flb_decode_fwd with a workspace)",
                 p->batch, p->heads, p->head_dim, splits, need, kStaticScratchBytes);
+  // num_splits stays as the caller gave it: with 0, flb_decode_fwd makes the same choices as
+  // for a workspace call (split count and, for a balanced launch, one CTA per SM), so both entry
+  // points compute the same partials.
   flb_decode_params q = *p;
-  q.num_splits = splits;
   q.workspace = nullptr;
   q.workspace_bytes = 0;
   if (need > 0) {

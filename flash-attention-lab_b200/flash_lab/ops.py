@@ -242,11 +242,14 @@ def _decode(q, k_cache, v_cache, seq_lens, softmax_scale: float, num_splits: int
         max_seqlen = block_tables.shape[1] * k_cache.shape[1]
         paged = (block_tables.data_ptr(), block_tables.stride(0), k_cache.shape[1],
                  k_cache.shape[0])
+    # abi_splits 0 lets the library choose (the same count as flb_decode_num_splits, and one CTA
+    # per SM for a length-balanced launch); the resolved count sizes the workspace.
     if not allow_splits:
-        splits = 1
+        splits = abi_splits = 1
     elif num_splits > 0:
-        splits = int(num_splits)
+        splits = abi_splits = int(num_splits)
     else:
+        abi_splits = 0
         splits = lib.flb_decode_num_splits(batch, heads, heads_kv, head_dim, max_seqlen,
                                            _sm_count(q.device))
     ws_bytes = lib.flb_decode_workspace_bytes(batch, heads, head_dim, splits)
@@ -260,7 +263,7 @@ def _decode(q, k_cache, v_cache, seq_lens, softmax_scale: float, num_splits: int
         k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
         v_cache.stride(0), v_cache.stride(1), v_cache.stride(2),
         o.stride(0), o.stride(1),
-        batch, heads, heads_kv, head_dim, max_seqlen, splits, _DECODE_DTYPE_CODE[q.dtype],
+        batch, heads, heads_kv, head_dim, max_seqlen, abi_splits, _DECODE_DTYPE_CODE[q.dtype],
         float(softmax_scale),
         0 if workspace is None else workspace.data_ptr(), ws_bytes,
         _status_ptr(q.device), *paged,

@@ -143,7 +143,7 @@ int flb_decode_num_splits(int32_t batch, int32_t heads, int32_t heads_kv, int32_
                           int32_t max_seqlen, int32_t sm_count);
 
 /* Bytes of device workspace flb_decode_fwd needs for this split count (0 when num_splits <= 1):
- * fp32 partials for batch * heads * (num_splits + 1) slots, (head_dim + 2) floats each.
+ * fp32 partials for batch * heads * (2 * num_splits + 1) slots, (head_dim + 2) floats each.
  * Replaces the per-call partial_o / partial_ml allocations (csrc/decode/decode.cu:303-311). */
 size_t flb_decode_workspace_bytes(int32_t batch, int32_t heads, int32_t head_dim,
                                   int32_t num_splits);
@@ -161,7 +161,7 @@ int flb_decode_fwd(const flb_decode_params* params, flb_stream_t stream);
  * flb_decode_fwd computes (the same kernels, the same split count), but keeps the split partials
  * in a static device array of flb_decode_static_scratch_bytes() bytes (8 MiB) instead of a
  * caller workspace; params->workspace is ignored. Problems whose partials do not fit
- * (flb_decode_workspace_bytes: B * H * (splits + 1) * (head_dim + 2) * 4 bytes, rounded) return
+ * (flb_decode_workspace_bytes: B * H * (2 * splits + 1) * (head_dim + 2) * 4 bytes, rounded) return
  * FLB_ERR_WORKSPACE without launching.
  * Every GPU that loads the library holds the array until exit. All calls on a device share it
  * and it keeps the last call's contents (nothing needs to start at zero), so calls that overlap

@@ -91,7 +91,7 @@ def test_split_count_depends_on_shapes_only(lib):
 def test_workspace_bytes(lib):
     assert lib.flb_decode_workspace_bytes(8, 32, 128, 1) == 0
     n = lib.flb_decode_workspace_bytes(8, 32, 128, 16)
-    slots = 8 * 32 * (16 + 1)   # a length-balanced launch writes up to B * H * (splits + 1)
+    slots = 8 * 32 * (2 * 16 + 1)   # a length-balanced launch writes up to B * H * (2 splits + 1)
     assert n >= slots * 128 * 4 + slots * 8
 
 

@@ -102,12 +102,15 @@ BALANCED = [
 ]
 
 
+@pytest.mark.parametrize("auto", [False, True], ids=["explicit", "auto"])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16],
                          ids=lambda d: str(d).removeprefix("torch."))
 @pytest.mark.parametrize("case", BALANCED, ids=lambda c: case_id(c) + f"-splits{c[6]}")
-def test_balanced_key_ranges(case, dtype):
+def test_balanced_key_ranges(case, dtype, auto):
+    # auto: the library's split count, and with it one CTA per SM (the deep K/V ring).
     gen = torch.Generator(device="cuda").manual_seed(9)
     *shape, splits = case
+    splits = None if auto else splits
     q, k_cache, v_cache, seq_lens = make_case(tuple(shape), dtype, gen)
     out, lse = flash_lab.decode(q, k_cache, v_cache, seq_lens, impl="splitkv",
                                 num_splits=splits, return_lse=True)
