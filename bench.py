@@ -44,6 +44,7 @@ sys.path.insert(0, str(ROOT / "flash-attention-lab_b200"))
 sys.path.insert(0, str(ROOT))
 
 PREFILL = dict(batch=4, heads=32, heads_kv=32, seqlen=4096, head_dim=128)
+E2E_Q_ROWS = 512   # query rows per host->device chunk of the e2e pipeline
 METRIC = "prefill TFLOP/s @(4,32,32,4096,128) bf16; decode HBM GB/s @32K cache"
 CPU_SAMPLE_ROWS = 1536
 REFERENCE_STEP_ROWS = 256
@@ -319,37 +320,55 @@ def main() -> int:
     hl = torch.empty((b, h, s), dtype=torch.float32).pin_memory()
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
 
-    # The step is pipelined over the batch, as a serving caller would run it: the host->device
-    # copy of sequence i+1 (copy stream), flash_lab.attention on sequence i (compute stream) and
-    # the device->host copy of sequence i-1 (second copy stream) overlap. Every byte still
-    # crosses PCIe inside the step, and the step ends when the last result is on the host.
+    # The step is pipelined as a serving caller would run it. Per sequence, its K and V go to
+    # the device (copy stream), then its queries in chunks of E2E_Q_ROWS rows; each chunk is
+    # attended against the full K / V (compute stream; non-causal rows are independent, so the
+    # chunks give the full result) and its output goes back to the host (second copy stream)
+    # while later chunks are still arriving. Small chunks keep the tail after the last
+    # host->device copy short. Every byte still crosses PCIe inside the step, and the step ends
+    # when the last result is on the host.
     s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    dl = torch.empty((b, h, s), device=device, dtype=torch.float32)
+    q_rows = min(E2E_Q_ROWS, s)
 
     def e2e_step():
         compute = torch.cuda.current_stream(device)
         s_in.wait_stream(compute)        # the previous step no longer reads dq, dk, dv
+        s_out.wait_stream(compute)       # nor is it copying out of dl
         for i in range(b):
             with torch.cuda.stream(s_in):
-                dq[i].copy_(hq[i], non_blocking=True)
                 dk[i].copy_(hk[i], non_blocking=True)
                 dv[i].copy_(hv[i], non_blocking=True)
-            compute.wait_stream(s_in)
-            o, lse = flash_lab.attention(dq[i:i + 1], dk[i:i + 1], dv[i:i + 1], causal=False,
-                                         softmax_scale=scale, return_lse=True)
-            s_out.wait_stream(compute)
+            for r0 in range(0, s, q_rows):
+                r1 = min(s, r0 + q_rows)
+                with torch.cuda.stream(s_in):
+                    dq[i, r0:r1].copy_(hq[i, r0:r1], non_blocking=True)
+                compute.wait_stream(s_in)
+                o, lse = flash_lab.attention(dq[i:i + 1, r0:r1], dk[i:i + 1], dv[i:i + 1],
+                                             causal=False, softmax_scale=scale, return_lse=True)
+                dl[i, :, r0:r1].copy_(lse[0])
+                s_out.wait_stream(compute)
+                with torch.cuda.stream(s_out):
+                    ho[i:i + 1, r0:r1].copy_(o, non_blocking=True)
+                o.record_stream(s_out)
             with torch.cuda.stream(s_out):
-                ho[i:i + 1].copy_(o, non_blocking=True)
-                hl[i:i + 1].copy_(lse, non_blocking=True)
-            o.record_stream(s_out)
-            lse.record_stream(s_out)
+                hl[i].copy_(dl[i], non_blocking=True)
         compute.wait_stream(s_out)       # the step ends with the last result on the host
 
     e2e_ms = time_steps(e2e_step, max(3, args.steps // 4), 3, dist, device)
+    # The pipelined step returns what one call on the whole resident batch returns, bit for bit.
+    o_full, lse_full = flash_lab.attention(q, k, v, causal=False, softmax_scale=scale,
+                                           return_lse=True)
+    torch.cuda.synchronize(device)
+    if not (torch.equal(ho, o_full.cpu()) and torch.equal(hl, lse_full.cpu())):
+        raise SystemExit("e2e: the pipelined step's host output differs from the full call")
+    del o_full, lse_full
     e2e = {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
            "ms_per_step": e2e_ms,
            "h2d_bytes_per_step": (hq.numel() + hk.numel() + hv.numel()) * 2,
            "d2h_bytes_per_step": ho.numel() * 2 + hl.numel() * 4,
-           "pipeline": "per sequence: h2d (copy stream) | attention (compute) | d2h (copy stream)"}
+           "pipeline": f"per sequence K/V, then {q_rows}-row query chunks: h2d (copy stream) | "
+                       "attention (compute) | d2h (copy stream)"}
 
     achieved = flops / (ms * 1e-3) / 1e12
     tr = traffic.get("prefill_kernel_noncausal")
