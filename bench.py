@@ -494,8 +494,8 @@ def run_extra(torch, flash_lab, device, dist, world, rank, args, peaks, traffic)
     # exchange (each rank's split kernel pushes its partials into every rank's buffer over
     # NVLink, then a bounded device wait and the fixed-order merge). decode_b1_split_allgather:
     # per-rank partials, NCCL all_gather, merge. On one rank both are the plain split decode.
-    from flash_lab import _capi
-    from flash_lab.distributed import PeerExchange, ShardSpec, decode_sharded
+    from flash_lab.distributed import (PeerExchange, ShardSpec, decode_sharded,
+                                       default_splits_per_rank)
 
     smax, hh, hk = 32768, 32, 32
     shard = ShardSpec.even(smax, world, rank)
@@ -508,7 +508,7 @@ def run_extra(torch, flash_lab, device, dist, world, rank, args, peaks, traffic)
     del full_k, full_v
     seq_lens = torch.full((1,), smax, device=device, dtype=torch.int32)
     sm = torch.cuda.get_device_properties(device).multi_processor_count
-    splits = _capi.load().flb_decode_num_splits(1, hh, hk, d, shard.length, sm)
+    splits = default_splits_per_rank(1, hh, hk, shard.length, sm)
     nbytes = decode_bytes(hh, hk, d, [smax], 1)
     # On one rank there is nothing to exchange: both lines time the local partials + merge.
     exchange = PeerExchange(1, hh, d, splits_per_rank=splits) if world > 1 else None

@@ -1287,6 +1287,12 @@ int splits_for(int batch, int heads, int heads_kv, int head_dim, int max_seqlen,
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>({by_sm, by_len, kMaxSplits})));
 }
 
+// A uniform launch of the 16-bit kernel (the sharded entry points) takes the deep ring when its
+// grid fits on the SMs at one CTA per SM.
+bool deep_fits(int grid_x, int grid_y, int sm_count) {
+  return static_cast<int64_t>(grid_x) * grid_y <= sm_count;
+}
+
 // Dynamic shared memory of a balanced launch of the 16-bit kernel.
 int balanced_smem(int head_dim, bool deep, int merge_rows) {
   if (head_dim == 128)
@@ -1467,7 +1473,8 @@ extern "C" int flb_decode_partials(const flb_decode_params* p, int32_t key_begin
   if (grid_y > 65535)
     return fail(FLB_ERR_UNSUPPORTED, "batch * heads_kv * head chunks = %d exceeds 65535", grid_y);
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
-  return launch_split_any(q.dtype, q.head_dim, a, tmk, tmv, q.num_splits, grid_y, stream);
+  return launch_split_any(q.dtype, q.head_dim, a, tmk, tmv, q.num_splits, grid_y, stream,
+                          deep_fits(q.num_splits, grid_y, sm_count));
 }
 
 extern "C" int flb_decode_merge(const float* partial_o, const float* partial_ml, int32_t batch,
@@ -1580,7 +1587,8 @@ extern "C" int flb_decode_partials_push(const flb_decode_params* p, int32_t key_
   if (grid_y > 65535)
     return fail(FLB_ERR_UNSUPPORTED, "batch * heads_kv * head chunks = %d exceeds 65535", grid_y);
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
-  return launch_split_any(q.dtype, q.head_dim, a, tmk, tmv, q.num_splits, grid_y, stream);
+  return launch_split_any(q.dtype, q.head_dim, a, tmk, tmv, q.num_splits, grid_y, stream,
+                          deep_fits(q.num_splits, grid_y, sm_count));
 }
 
 extern "C" int flb_decode_merge_peers(const flb_peer_exchange* x, int32_t parity,

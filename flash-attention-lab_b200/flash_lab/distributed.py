@@ -65,6 +65,15 @@ def local_lengths(seq_lens: torch.Tensor, shard: ShardSpec) -> torch.Tensor:
     return (seq_lens - shard.offset).clamp_(0, shard.length).to(torch.int32).contiguous()
 
 
+def default_splits_per_rank(batch: int, heads: int, heads_kv: int, shard_length: int,
+                            sm_count: int) -> int:
+    """Key splits per rank for decode_sharded: one CTA per SM (the sharded kernels then run
+    their deeper K/V ring), and splits of at least 512 keys. A function of shapes only, so the
+    same on every rank and valid inside a captured graph."""
+    units = batch * heads_kv * -(-(heads // heads_kv) // 16)
+    return max(1, min(sm_count // max(units, 1), shard_length // 512))
+
+
 def _dtype_code(dtype: torch.dtype) -> int:
     if dtype == torch.bfloat16:
         return _capi.FLB_BF16
