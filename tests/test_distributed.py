@@ -23,7 +23,8 @@ import torch.multiprocessing as mp
 
 import oracle
 from flash_lab import _capi
-from flash_lab.distributed import ShardSpec, decode_sharded, local_lengths, merge_partials
+from flash_lab.distributed import (ShardSpec, decode_sharded, default_splits_per_rank,
+                                   local_lengths, merge_partials)
 
 TILE = 64  # keys per decode tile: split ranges are whole numbers of tiles
 
@@ -120,6 +121,16 @@ def test_shards_cover_the_sequence():
     lens = torch.tensor([0, 10, 600, 1000], dtype=torch.int32)
     got = local_lengths(lens, ShardSpec(334, 333))
     assert got.tolist() == [0, 0, 266, 333]
+
+
+def test_default_splits_per_rank():
+    # One CTA per SM over batch * KV heads * head chunks, splits of at least 512 keys.
+    assert default_splits_per_rank(1, 32, 32, 16384, 148) == 4
+    assert default_splits_per_rank(1, 32, 32, 4096, 148) == 4
+    assert default_splits_per_rank(1, 32, 32, 1000, 148) == 1
+    assert default_splits_per_rank(8, 32, 8, 32768, 148) == 2
+    assert default_splits_per_rank(1, 64, 2, 4096, 148) == 8     # group 32: two head chunks
+    assert default_splits_per_rank(64, 32, 8, 32768, 148) == 1   # more units than SMs
 
 
 def _window_partials(q3, kc, vc, lens, key_begin, key_end, splits, scale):
