@@ -6,17 +6,20 @@
 // csrc/common/params.h:31-53.
 //
 // B200 design (not a port):
-//  * One CTA = (sequence b, KV head, <=16 query heads of its GQA group, key split). Every query
-//    head that shares the KV head is served by the same CTA, so GQA reads each K/V byte once.
+//  * One CTA = (KV head, <=16 query heads of its GQA group) and a range of keys: one sequence's
+//    key split (uniform launch), or an equal share of the batch's 64-key chunks that may span
+//    sequences (length-balanced launch, see balanced_prefix). Every query head that shares the
+//    KV head is served by the same CTA, so GQA reads each K/V byte once.
 //  * A producer warp streams 64-key K and V tiles with TMA (128-byte swizzled boxes of
-//    [64 keys x 64 dims]) into a STAGES-deep mbarrier ring; the strided cache is described by a
-//    4-D tensor map, so any row stride (native [B,S,H,D] or the HF [B,H,S,D] static-cache view)
-//    is read in place.
+//    [64 keys x 64 dims]) into an mbarrier ring (3 stages, or 4 when a launch has one CTA per
+//    SM); the strided cache is described by a 4-D tensor map, so any row stride (native
+//    [B,S,H,D] or the HF [B,H,S,D] static-cache view) is read in place.
 //  * Four consumer warps each take 16 keys of every tile. The group's query heads are the M rows
 //    of a 16x8x16 warp MMA (rows beyond the group are zero), so Q K^T and P V are tiny tensor-core
 //    GEMMs and the fp32 online softmax (exp2 domain) stays in registers.
-//  * Partial results of the four warps, and then of the splits, are merged in a fixed order, so a
-//    given configuration is bitwise reproducible.
+//  * Partial results of the four warps, and then of the splits (or, in a balanced launch, of the
+//    CTAs that hold a sequence's chunks), are merged in a fixed order, so a given configuration
+//    is bitwise reproducible.
 //  * seq_lens is read on the device only and clamped to [0, S_max]; keys past a sequence's length
 //    get probability 0 and their V values are masked out of the product (unused cache rows may
 //    hold anything, NaN included).
@@ -257,6 +260,29 @@ __device__ __forceinline__ int sequence_of_chunk(const int* pref, int batch, int
   }
   return lo;
 }
+
+// g(c) = floor(c N / T) for consecutive c without a division per step: start() divides once,
+// step() moves to c + 1 and returns g(c + 1).
+struct ChunkWalk {
+  int64_t g, r, q_step, r_step, total;
+  __device__ __forceinline__ void start(int c, int64_t n, int t) {
+    total = t;
+    const int64_t cn = static_cast<int64_t>(c) * n;
+    g = cn / t;
+    r = cn - g * t;
+    q_step = n / t;
+    r_step = n - q_step * t;
+  }
+  __device__ __forceinline__ int64_t step() {
+    g += q_step;
+    r += r_step;
+    if (r >= total) {
+      r -= total;
+      ++g;
+    }
+    return g;
+  }
+};
 
 // True on every one of the 128 consumer threads when pred holds on any of them (named barrier
 // 1 with an OR reduction), so that all of them take the same branch after it.
@@ -973,7 +999,7 @@ __global__ void decode_merge_balanced_kernel(const float* __restrict__ partial_o
   __shared__ int lens[kMaxBalancedBatch];
   if (threadIdx.x < 32) balanced_prefix(seq_lens, batch, 0, max_seqlen, pref, lens, threadIdx.x);
   __syncthreads();
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // Everything that depends on the lengths only is done before waiting for the split kernel.
   const int bh = blockIdx.x;
   const int b = bh / heads;
   const int h = bh - b * heads;
@@ -981,23 +1007,31 @@ __global__ void decode_merge_balanced_kernel(const float* __restrict__ partial_o
   const int64_t p0 = pref[b], p1 = pref[b + 1];
   // CTAs holding chunks p0 and p1 - 1: CTA c holds chunk x when c = floor(((x + 1) T - 1) / N).
   int c_first = 0, c_last = -1;
+  ChunkWalk walk0{};
   if (p1 > p0) {
     c_first = static_cast<int>(((p0 + 1) * total - 1) / n);
     c_last = static_cast<int>((p1 * total - 1) / n);
+    walk0.start(c_first, n, total);
   }
-  auto holds = [&](int c) {   // CTA c holds at least one chunk of sequence b
-    const int64_t g0 = static_cast<int64_t>(c) * n / total;
-    const int64_t g1 = static_cast<int64_t>(c + 1) * n / total;
-    return max(g0, p0) < min(g1, p1);
-  };
   const int64_t base = static_cast<int64_t>(h) * (batch + total) + b;   // + c: CTA c's slot
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // CTA c (chunks [g(c), g(c + 1))) holds part of sequence b when that range meets [p0, p1).
   float m = -INFINITY;
-  for (int c = c_first; c <= c_last; ++c)
-    if (holds(c)) m = fmaxf(m, partial_ml[2 * (base + c)]);
+  {
+    ChunkWalk w = walk0;
+    for (int c = c_first; c <= c_last; ++c) {
+      const int64_t g0 = w.g;
+      const int64_t g1 = w.step();
+      if (max(g0, p0) < min(g1, p1)) m = fmaxf(m, partial_ml[2 * (base + c)]);
+    }
+  }
   for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
     float num = 0.f, den = 0.f;
+    ChunkWalk w = walk0;
     for (int c = c_first; c <= c_last; ++c) {
-      if (!holds(c)) continue;
+      const int64_t g0 = w.g;
+      const int64_t g1 = w.step();
+      if (!(max(g0, p0) < min(g1, p1))) continue;
       const float ms = partial_ml[2 * (base + c)];
       if (ms != -INFINITY) {
         const float f = ex2(ms - m);
