@@ -23,6 +23,7 @@ import os
 from dataclasses import dataclass
 
 import torch
+from torch.utils import _python_dispatch
 
 from flash_lab import _capi
 from flash_lab.layouts import AttnShape, DecodeShape, check_attention_inputs, check_decode_inputs
@@ -155,6 +156,13 @@ def _sm_count(device: torch.device) -> int:
     return n
 
 
+def _raw_stream(device: torch.device) -> int:
+    """The current CUDA stream of `device` as a cudaStream_t value (without building a Stream
+    object)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    return torch._C._cuda_getCurrentRawStream(idx)
+
+
 def _require_library() -> ctypes.CDLL:
     if _LIB is None:
         raise RuntimeError(f"the sm_100a library did not load: {EXTENSION_ERROR}")
@@ -215,7 +223,7 @@ def _prefill(q, k, v, causal: bool, softmax_scale: float):
     if q.stride(-1) != 1 or k.stride(-1) != 1 or v.stride(-1) != 1:
         raise RuntimeError("q, k, v must be contiguous in head_dim")
     with _DeviceGuard(q.device):
-        status = lib.flb_prefill_fwd(ctypes.byref(p), torch.cuda.current_stream(q.device).cuda_stream)
+        status = lib.flb_prefill_fwd(ctypes.byref(p), _raw_stream(q.device))
     _check(status, "flb_prefill_fwd", q.device)
     return o, lse
 
@@ -269,7 +277,7 @@ def _decode(q, k_cache, v_cache, seq_lens, softmax_scale: float, num_splits: int
         _status_ptr(q.device), *paged,
     )
     with _DeviceGuard(q.device):
-        status = lib.flb_decode_fwd(ctypes.byref(p), torch.cuda.current_stream(q.device).cuda_stream)
+        status = lib.flb_decode_fwd(ctypes.byref(p), _raw_stream(q.device))
     _check(status, "flb_decode_fwd", q.device)
     return o, lse
 
@@ -290,7 +298,12 @@ def _decode_paged_fake(q, k_cache, v_cache, seq_lens, block_tables, softmax_scal
 _LIBRARIES: list = []  # keeps the torch.library fragments alive
 
 
+# The Python implementation behind each registered op, for the eager fast path (_call_op).
+_EAGER_IMPLS: dict[str, object] = {}
+
+
 def _define(name: str, schema: str, impl, fake) -> None:
+    _EAGER_IMPLS[name] = impl
     if hasattr(torch.ops.flash_lab, name):
         return
     lib = torch.library.Library("flash_lab", "FRAGMENT")
@@ -324,6 +337,45 @@ _BUILT_OPS = frozenset(
     spec.op for spec in (*PREFILL_IMPLS.values(), *DECODE_IMPLS.values())
     if HAS_EXTENSION and hasattr(torch.ops.flash_lab, spec.op)
 )
+
+
+def _eager_ok(args) -> bool:
+    """Plain tensors, eager mode, no torch function or dispatch mode active."""
+    if torch.compiler.is_compiling() or torch._C._is_torch_function_mode_enabled():
+        return False
+    if _python_dispatch._get_current_dispatch_mode() is not None:
+        return False
+    return all(type(a) is torch.Tensor for a in args if isinstance(a, torch.Tensor))
+
+
+def _call_op(name: str, *args):
+    """Runs torch.ops.flash_lab.<name>. torch.compile, tensor subclasses and torch modes go
+    through the registered op; plain eager calls run the same implementation directly, without
+    the dispatcher's cost (about 4 us per call)."""
+    if _eager_ok(args):
+        return _EAGER_IMPLS[name](*args)
+    return getattr(torch.ops.flash_lab, name)(*args)
+
+
+_SELECTED: dict[tuple, object] = {}
+
+
+def _select_cached(kind: str, table: dict, impl: str, device: torch.device, key: tuple,
+                   describe, reason_of):
+    """_select, memoised on (table, impl, device type, key) once it has succeeded (key holds
+    every input of reason_of: the shape, the dtype and, for prefill, causal). Failures are not
+    cached, so errors come from _select in its order. Under torch.compile the selection is
+    traced as written (it folds to a constant)."""
+    if torch.compiler.is_compiling():
+        return _select(table, impl, device, describe, reason_of)
+    full = (kind, impl, device.type, key)
+    spec = _SELECTED.get(full)
+    if spec is None:
+        spec = _select(table, impl, device, describe, reason_of)
+        if len(_SELECTED) >= 4096:   # many distinct shapes: start over rather than grow
+            _SELECTED.clear()
+        _SELECTED[full] = spec
+    return spec
 
 
 def available_impls() -> dict[str, list[str]]:
@@ -367,13 +419,13 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = 
     scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(shape.head_dim)
     if not scale > 0:
         raise ValueError(f"softmax_scale must be positive, got {scale}")
-    spec = _select(
-        PREFILL_IMPLS, impl, q.device,
+    spec = _select_cached(
+        "attention", PREFILL_IMPLS, impl, q.device, (shape, q.dtype, bool(causal)),
         lambda: (f"dtype={q.dtype}, head_dim={shape.head_dim}, heads={shape.heads}/"
                  f"{shape.heads_kv}, S_q={shape.seqlen_q}, S_k={shape.seqlen_k}, causal={causal}"),
         lambda s: s.unsupported_reason(shape, q.dtype, causal),
     )
-    out, lse = getattr(torch.ops.flash_lab, spec.op)(q, k, v, causal, scale)
+    out, lse = _call_op(spec.op, q, k, v, causal, scale)
     return (out, lse) if return_lse else out
 
 
@@ -392,19 +444,17 @@ def decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, seq_le
     scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(shape.head_dim)
     if num_splits is not None and num_splits < 1:
         raise ValueError(f"num_splits must be positive, got {num_splits}")
-    spec = _select(
-        DECODE_IMPLS, impl, q.device,
+    spec = _select_cached(
+        "decode", DECODE_IMPLS, impl, q.device, (shape, q.dtype),
         lambda: (f"dtype={q.dtype}, head_dim={shape.head_dim}, heads={shape.heads}/"
                  f"{shape.heads_kv}, paged={shape.paged}"),
         lambda s: s.unsupported_reason(shape, q.dtype),
     )
     if block_tables is None:
-        out, lse = getattr(torch.ops.flash_lab, spec.op)(q3, k_cache, v_cache, seq_lens, scale,
-                                                         num_splits or 0)
+        out, lse = _call_op(spec.op, q3, k_cache, v_cache, seq_lens, scale, num_splits or 0)
     else:
-        out, lse = getattr(torch.ops.flash_lab, spec.paged_op)(q3, k_cache, v_cache, seq_lens,
-                                                               block_tables, scale,
-                                                               num_splits or 0)
+        out, lse = _call_op(spec.paged_op, q3, k_cache, v_cache, seq_lens, block_tables, scale,
+                            num_splits or 0)
     if q.dim() == 4:
         out = out.unsqueeze(1)
     return (out, lse) if return_lse else out
