@@ -340,8 +340,11 @@ _BUILT_OPS = frozenset(
 
 
 def _eager_ok(args) -> bool:
-    """Plain tensors, eager mode, no torch function or dispatch mode active."""
+    """Plain tensors, eager mode, no torch function or dispatch mode active, no profiler (which
+    then records the flash_lab:: op by name)."""
     if torch.compiler.is_compiling() or torch._C._is_torch_function_mode_enabled():
+        return False
+    if torch.autograd._profiler_enabled():
         return False
     if _python_dispatch._get_current_dispatch_mode() is not None:
         return False
