@@ -163,3 +163,41 @@ def test_c_abi_error_status_becomes_runtime_error(monkeypatch):
     with pytest.raises(RuntimeError, match="flb_decode_fwd: CUDA error: injected launch failure"):
         ops._check(_capi.FLB_ERR_CUDA, "flb_decode_fwd", torch.device("cpu"))
     ops._check(_capi.FLB_OK, "flb_decode_fwd", torch.device("cpu"))   # OK passes silently
+
+
+@pytest.mark.gpu
+def test_eager_fast_path_matches_the_registered_ops():
+    # Plain eager calls run the op's implementation directly; the registered op gives the same
+    # bits, and a torch dispatch mode still sees the flash_lab:: ops by name.
+    from torch.utils._python_dispatch import TorchDispatchMode
+
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    q = torch.randn(1, 300, 4, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+    k = torch.randn(1, 300, 2, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+    v = torch.randn(1, 300, 2, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+    o, lse = flash_lab.attention(q, k, v, causal=True, return_lse=True)
+    o_op, lse_op = torch.ops.flash_lab.attention_sm100(q, k, v, True, 128 ** -0.5)
+    assert torch.equal(o, o_op) and torch.equal(lse, lse_op)
+
+    qd = torch.randn(2, 8, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+    kc = torch.randn(2, 3000, 2, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+    vc = torch.randn(2, 3000, 2, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+    lens = torch.tensor([3000, 1234], device="cuda", dtype=torch.int32)
+    od, lsed = flash_lab.decode(qd, kc, vc, lens, return_lse=True)
+    od_op, lsed_op = torch.ops.flash_lab.decode_splitkv(qd, kc, vc, lens, 128 ** -0.5, 0)
+    assert torch.equal(od, od_op) and torch.equal(lsed, lsed_op)
+
+    class Record(TorchDispatchMode):
+        def __init__(self):
+            super().__init__()
+            self.names = []
+
+        def __torch_dispatch__(self, func, types, args=(), kwargs=None):
+            self.names.append(str(func))
+            return func(*args, **(kwargs or {}))
+
+    with Record() as rec:
+        flash_lab.attention(q, k, v, causal=True)
+        flash_lab.decode(qd, kc, vc, lens)
+    assert any("flash_lab.attention_sm100" in n for n in rec.names), rec.names
+    assert any("flash_lab.decode_splitkv" in n for n in rec.names), rec.names
