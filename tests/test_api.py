@@ -201,3 +201,35 @@ def test_eager_fast_path_matches_the_registered_ops():
         flash_lab.decode(qd, kc, vc, lens)
     assert any("flash_lab.attention_sm100" in n for n in rec.names), rec.names
     assert any("flash_lab.decode_splitkv" in n for n in rec.names), rec.names
+
+
+def test_eager_fast_path_only_for_plain_eager_calls():
+    # The direct call is taken for plain tensors only; torch modes and tensor subclasses (and
+    # torch.compile, which traces flash_lab.attention / decode) go through the registered ops.
+    from torch.overrides import TorchFunctionMode
+    from torch.utils._python_dispatch import TorchDispatchMode
+
+    from flash_lab import ops
+
+    x = torch.zeros(2)
+    assert ops._eager_ok((x, 1.0, 3))
+
+    class Sub(torch.Tensor):
+        pass
+
+    assert not ops._eager_ok((x.as_subclass(Sub), 1.0))
+
+    class Dispatch(TorchDispatchMode):
+        def __torch_dispatch__(self, func, types, args=(), kwargs=None):
+            return func(*args, **(kwargs or {}))
+
+    with Dispatch():
+        assert not ops._eager_ok((x,))
+
+    class Function(TorchFunctionMode):
+        def __torch_function__(self, func, types, args=(), kwargs=None):
+            return func(*args, **(kwargs or {}))
+
+    with Function():
+        assert not ops._eager_ok((x,))
+    assert ops._eager_ok((x,))
