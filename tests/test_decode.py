@@ -123,6 +123,18 @@ def test_balanced_key_ranges(case, dtype, auto):
     check_decode(out[keep], lse[keep], q[keep], k_cache[keep], v_cache[keep], lens[keep])
 
 
+@pytest.mark.parametrize("num_splits", [2, None], ids=["splits2", "auto"])
+@pytest.mark.parametrize("batch", [128, 130])
+def test_balanced_launch_batch_limit(batch, num_splits):
+    # Up to 128 sequences take the length-balanced launch; more take the uniform split.
+    gen = torch.Generator(device="cuda").manual_seed(10)
+    q, k_cache, v_cache, seq_lens = make_case((batch, 8, 1, 2048, 64, "random"), torch.bfloat16,
+                                              gen)
+    out, lse = flash_lab.decode(q, k_cache, v_cache, seq_lens, impl="splitkv",
+                                num_splits=num_splits, return_lse=True)
+    check_decode(out, lse, q, k_cache, v_cache, seq_lens)
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32],
                          ids=lambda d: str(d).removeprefix("torch."))
 @pytest.mark.parametrize("impl", IMPLS)
