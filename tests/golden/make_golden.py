@@ -3,7 +3,9 @@
 Run once in a container that has the reference checked out (it imports the real
 flash_lab.reference, pure PyTorch, on the CPU):
 
-    PYTHONPATH=<reference checkout> python tests/golden/make_golden.py
+    PYTHONPATH=<reference checkout> python tests/golden/make_golden.py [case ...]
+
+With case names, only those fixtures are rewritten (the manifest always lists every case).
 
 For each case it draws seeded N(0, 1) inputs with torch's CPU generator, rounds them to bf16 (the
 dtype the kernels run in), calls flash_lab.reference (attention, attention_rows, attention_tiled,
@@ -39,9 +41,11 @@ def main() -> int:
         return 1
 
     manifest = {}
+    only = set(sys.argv[1:])
 
     def save(name, meta, **arrays):
-        np.savez_compressed(HERE / f"{name}.npz", **arrays)
+        if not only or name in only:
+            np.savez_compressed(HERE / f"{name}.npz", **arrays)
         manifest[name] = meta
 
     # C0, the BASELINE CPU-plumbing config: B=1, H=H_kv=4, S=256, D=64, scale 1/8.
@@ -104,12 +108,15 @@ def main() -> int:
     save("rows_tiled", {"kind": "rows_tiled", "shape": [2, 70, 50, 4, 2, 16]},
          q=bf16_bits(q), k=bf16_bits(k), v=bf16_bits(v), rows=rows.numpy(), **extra)
 
-    # Decode cases from tests/test_decode.py:232-240 (the small ones) and a GQA-4 case.
+    # Decode cases from tests/test_decode.py:232-240 (the small ones), a GQA-4 case, and a
+    # ragged batch long enough for several splits (on B200 a length-balanced launch, whose CTAs
+    # hold parts of several short sequences).
     decode_cases = [
         (1, 8, 8, 64, 64, [64]),
         (2, 6, 2, 300, 64, [300, 17]),
         (4, 8, 1, 260, 128, [1, 5, 129, 260]),
         (3, 16, 4, 120, 128, [120, 40, 77]),
+        (6, 4, 1, 1100, 64, [1100, 1, 3, 64, 700, 65]),
     ]
     for i, (b, h, hkv, smax, d, lens) in enumerate(decode_cases):
         gen = torch.Generator().manual_seed(200 + i)
