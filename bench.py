@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-extra]
 
-Headline workload (BASELINE prefill config): bf16 prefill forward, (B, H, H_kv, S, D) =
+Headline workload (the benchmark's prefill configuration): bf16 prefill forward, (B, H, H_kv, S, D) =
 (4, 32, 32, 4096, 128), non-causal, Q/K/V ~ N(0, 1) from a seed, scale 1/sqrt(128). One step is
 one flash_lab.attention call over that batch; metric TFLOP/s counts 4*B*H*S_q*S_k*D FLOP per
 call (the reference's bench/flops.py convention). Inputs (402 MB) are larger than the 126 MB L2,
@@ -257,7 +257,7 @@ def main() -> int:
                     help="run only warmup + steps launches of one kernel (for ncu captures)")
     ap.add_argument("--batch", type=int, default=None, help="batch size of --profile")
     ap.add_argument("--e2e-llama", action="store_true",
-                    help="end-to-end Llama-3.1-8B-architecture generation (BASELINE config 5)")
+                    help="end-to-end Llama-3.1-8B-architecture generation (the e2e configuration)")
     ap.add_argument("--new-tokens", type=int, default=256)
     ap.add_argument("--prompt-len", type=int, default=8192)
     args = ap.parse_args()
@@ -559,7 +559,7 @@ def run_extra(torch, flash_lab, device, dist, world, rank, args, peaks, traffic)
 
 
 def run_e2e_llama(args) -> int:
-    """Llama-3.1-8B architecture (32 layers, d_model 4096, 32 heads, 8 KV
+    """The e2e configuration: Llama-3.1-8B architecture (32 layers, d_model 4096, 32 heads, 8 KV
     heads, head_dim 128, RoPE theta 500000, vocab 128256) with random-init bf16 weights, batch 1,
     a random 8192-token prompt, 256 greedy tokens, a static KV cache and the decode step compiled
     (torch.compile fullgraph, CUDA graphs), attention through the flash_lab HF backend; the same

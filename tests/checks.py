@@ -7,7 +7,7 @@ reference's fp32 floors 1e-6 / 1e-5):
         err <= 2 * err_torch + FLOOR   (err_torch: PyTorch's own computation at the input dtype)
         err <= GUARD * (1 + max|v|)    (prefill)
         lse_err <= 2 * lse_err_torch + LSE_FLOOR, and lse is -inf exactly where the oracle's is;
-  * the BASELINE rule of this build's north star:
+  * the stricter rounding rule of the benchmark's parity target:
         err <= 2 * max|round_dtype(ref64) - ref64|
     i.e. the kernel's output error is at most twice that of the fp64 reference rounded to the
     output dtype.

@@ -48,7 +48,7 @@ def main() -> int:
             np.savez_compressed(HERE / f"{name}.npz", **arrays)
         manifest[name] = meta
 
-    # C0, the BASELINE CPU-plumbing config: B=1, H=H_kv=4, S=256, D=64, scale 1/8.
+    # C0, the benchmark's CPU-plumbing configuration: B=1, H=H_kv=4, S=256, D=64, scale 1/8.
     gen = torch.Generator().manual_seed(0)
     q, k, v = rnd(gen, 1, 256, 4, 64), rnd(gen, 1, 256, 4, 64), rnd(gen, 1, 256, 4, 64)
     outs = {}

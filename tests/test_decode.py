@@ -2,7 +2,7 @@
 and the reference's golden vectors. Cases follow the reference's tests/test_decode.py: ragged
 lengths, length 1, GQA groups 4 and 8, random lengths, split counts with empty splits, strided
 caches, rank-3 queries, determinism, rejections; plus poisoned unused cache rows, lengths outside
-[1, S_max] (clamped on the device) and the BASELINE 32K configurations checked on slices."""
+[1, S_max] (clamped on the device) and the benchmark's 32K configurations checked on slices."""
 
 import numpy as np
 import pytest
@@ -246,7 +246,7 @@ def _check_slices(out, lse, q, k_cache, v_cache, seq_lens, picks):
 
 
 def test_baseline_mha_32k():
-    """BASELINE decode config: B=8, H=H_kv=32, D=128, S_max=32768, all lengths 32768."""
+    """The benchmark's MHA decode configuration: B=8, H=H_kv=32, D=128, S_max=32768, all 32768."""
     gen = torch.Generator(device="cuda").manual_seed(10)
     q, k_cache, v_cache, _ = make_case((8, 32, 32, 32768, 128, [1] * 8), torch.bfloat16, gen)
     seq_lens = torch.full((8,), 32768, device="cuda", dtype=torch.int32)
@@ -255,7 +255,7 @@ def test_baseline_mha_32k():
 
 
 def test_baseline_gqa_32k_ragged():
-    """BASELINE GQA config: B=8, H=32, H_kv=8, lengths U[16384, 32768] from a seed."""
+    """The benchmark's GQA decode configuration: B=8, H=32, H_kv=8, lengths U[16384, 32768]."""
     gen = torch.Generator(device="cuda").manual_seed(11)
     q, k_cache, v_cache, _ = make_case((8, 32, 8, 32768, 128, [1] * 8), torch.bfloat16, gen)
     seq_lens = torch.randint(16384, 32769, (8,), generator=torch.Generator().manual_seed(0))

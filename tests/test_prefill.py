@@ -2,7 +2,7 @@
 numpy oracle and the reference's golden vectors. Cases follow the reference's
 tests/test_attention_fwd.py: ragged lengths, S_q != S_k with bottom-right causal masking, rows
 without keys, GQA, large scores, strided packed-QKV views, determinism and rejections; plus the
-BASELINE prefill configuration (4, 32, 32, 4096, 128) checked on sampled rows."""
+benchmark's prefill configuration (4, 32, 32, 4096, 128) checked on sampled rows."""
 
 import numpy as np
 import pytest
@@ -156,7 +156,7 @@ def _misaligned(x):
 
 @pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
 def test_baseline_config_sampled_rows(causal):
-    """BASELINE prefill config (B, H, H_kv, S, D) = (4, 32, 32, 4096, 128), checked on 256 rows
+    """The benchmark's prefill configuration (B, H, H_kv, S, D) = (4, 32, 32, 4096, 128), on 256 rows
     (first, last and 254 random ones, as the reference's bench/run.py:75-80)."""
     q, k, v = make_inputs((4, 4096, 4096, 32, 32, 128), torch.bfloat16, seed=1)
     out, lse = flash_lab.attention(q, k, v, causal=causal, return_lse=True)
