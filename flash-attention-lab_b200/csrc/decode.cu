@@ -63,6 +63,11 @@ struct DecodeArgs {
   float* partial_ml[kMaxDest];
   unsigned long long* arrive[kMaxDest];
   unsigned int* cta_done;
+  // Peer push: this rank's completed-step count (in its own exchange buffer) selects the parity
+  // region; partials of parity 1 sit region_o / region_ml floats after those of parity 0. Null
+  // outside a push (region 0 only).
+  const unsigned long long* step_word;
+  int64_t region_o, region_ml;
   // Paged cache: block table [B, max_blocks] (row stride bt_stride), page_size rows per block,
   // and box_rows, the rows of one TMA box (a box never crosses a page). Null for a contiguous
   // cache, whose "block" is the sequence and whose box covers a whole tile.
@@ -306,6 +311,13 @@ __device__ __forceinline__ bool consumers_any(bool pred) {
 // local or over NVLink, visible to a rank that acquires the counter. It then resets the count
 // for the next launch (launches on one stream do not overlap). A contended system-scope atomic
 // per CTA cost tens of microseconds, a system-scope fence per CTA about ten.
+// A push whose status word is already nonzero (an earlier step's wait timed out, or one of this
+// launch's own pipeline waits) publishes nothing: the other ranks' merges then time out too, so
+// every rank's exchange ends in the failed state instead of one of them merging stale partials.
+__device__ __forceinline__ bool push_failed(const DecodeArgs& a) {
+  return a.status != nullptr && *reinterpret_cast<volatile const int*>(a.status) != 0;
+}
+
 __device__ __forceinline__ void publish_push(const DecodeArgs& a) {
   __threadfence();
   const unsigned int total = gridDim.x * gridDim.y;
@@ -314,7 +326,9 @@ __device__ __forceinline__ void publish_push(const DecodeArgs& a) {
     // (a release add per destination would fence once per destination).
     __threadfence_system();
     *a.cta_done = 0u;
-    for (int dst = 0; dst < a.n_dest; ++dst) red_relaxed_sys_add(a.arrive[dst], 1ull);
+    if (!push_failed(a)) {
+      for (int dst = 0; dst < a.n_dest; ++dst) red_relaxed_sys_add(a.arrive[dst], 1ull);
+    }
   }
 }
 
@@ -340,7 +354,19 @@ __device__ __forceinline__ void finish_split(const DecodeArgs& a, const float* w
                                              const float* wo, int heads_here, int head0, int b,
                                              int64_t seg_slot, int64_t h_stride, int mrows) {
   const int tid = threadIdx.x;
-  for (int idx = tid; idx < heads_here * D; idx += kDecodeConsumerWarps * 32) {
+  // A push writes the parity region of this rank's step count, and nothing once the exchange
+  // has failed.
+  int64_t off_o = 0, off_ml = 0;
+  bool skip = false;
+  if (a.step_word != nullptr) {
+    if (*reinterpret_cast<volatile const unsigned long long*>(a.step_word) & 1ull) {
+      off_o = a.region_o;
+      off_ml = a.region_ml;
+    }
+    skip = push_failed(a);
+  }
+  for (int idx = skip ? heads_here * D : tid; idx < heads_here * D;
+       idx += kDecodeConsumerWarps * 32) {
     const int row = idx / D;
     const int d = idx - row * D;
     float m = -INFINITY;
@@ -368,10 +394,10 @@ __device__ __forceinline__ void finish_split(const DecodeArgs& a, const float* w
     } else {
       const int64_t slot = seg_slot + h * h_stride;
       for (int dst = 0; dst < a.n_dest; ++dst) {
-        a.partial_o[dst][slot * D + d] = num;
+        a.partial_o[dst][off_o + slot * D + d] = num;
         if (d == 0) {
-          a.partial_ml[dst][2 * slot] = m;
-          a.partial_ml[dst][2 * slot + 1] = den;
+          a.partial_ml[dst][off_ml + 2 * slot] = m;
+          a.partial_ml[dst][off_ml + 2 * slot + 1] = den;
         }
       }
     }
@@ -919,11 +945,17 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
                          a.splits_total, kMaxHeadsPerCta);
 }
 
-// Arrivals a merge waits for: counters[src] >= expected for every source rank (null = none).
+// A peer merge's view of this rank's exchange buffer (null counters = a plain merge): the
+// arrival counters of every source rank, this rank's completed-step count n and the CTA count of
+// the merge in progress. Step n merges parity region n % 2 (partials region_o / region_ml floats
+// past those of region 0 when it is 1) once every counter has reached n + 1; the last CTA to
+// finish then advances n. Both live in device memory, so a captured CUDA graph replays steps.
 struct PeerWait {
   const unsigned long long* counters;
+  unsigned long long* step_word;
+  unsigned int* merge_done;
   int world;
-  unsigned long long expected;
+  int64_t region_o, region_ml;
   int64_t timeout_ns;
   int* status;
 };
@@ -931,7 +963,9 @@ struct PeerWait {
 // Fixed-order merge of the split partials of one (b, h): thread d owns output column d.
 // m = max_s m_s; l = sum_s l_s 2^(m_s - m); o = sum_s o_s 2^(m_s - m) / l (empty splits skipped).
 // kPeers: the partials are written by other GPUs; thread 0 first waits (bounded) for every
-// source's arrival counter, and the partials are read through L2 (ld.global.cg).
+// source's arrival counter, and the partials are read through L2 (ld.global.cg). A wait that
+// times out, or an exchange whose status word is already nonzero, writes NaN to o and lse (the
+// exchange stays failed until the ranks reset it together).
 template <typename T, bool kPeers>
 __global__ void decode_merge_kernel(const float* __restrict__ partial_o,
                                     const float* __restrict__ partial_ml, int heads, int head_dim,
@@ -940,14 +974,20 @@ __global__ void decode_merge_kernel(const float* __restrict__ partial_o,
   // Launched as a programmatic dependent of the split kernel: wait for its writes first (a no-op
   // when launched normally).
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int bh = blockIdx.x;
+  const int b = bh / heads;
+  const int h = bh - b * heads;
   if constexpr (kPeers) {
     __shared__ int s_failed;
+    __shared__ unsigned long long s_step;
     if (threadIdx.x == 0) {
-      int failed = 0;
+      int failed = wait.status != nullptr && *reinterpret_cast<volatile int*>(wait.status) != 0;
+      const unsigned long long n =
+          *reinterpret_cast<volatile const unsigned long long*>(wait.step_word);
       const uint64_t start = global_timer_ns();
       for (int src = 0; src < wait.world && !failed; ++src) {
         uint32_t polls = 0;
-        while (ld_relaxed_sys_u64(wait.counters + src) < wait.expected) {
+        while (ld_relaxed_sys_u64(wait.counters + src) < n + 1) {
           if (((++polls) & 63u) == 0 &&
               global_timer_ns() - start > static_cast<uint64_t>(wait.timeout_ns)) {
             failed = 1;
@@ -958,14 +998,30 @@ __global__ void decode_merge_kernel(const float* __restrict__ partial_o,
       }
       fence_acq_rel_sys();   // the partials the counters announce are visible from here on
       s_failed = failed;
+      s_step = n;
     }
     __syncthreads();
+    const unsigned long long n = s_step;
+    if (n & 1ull) {
+      partial_o += wait.region_o;
+      partial_ml += wait.region_ml;
+    }
+    if (s_failed) {
+      T* out = o + static_cast<int64_t>(b) * o_batch_stride + static_cast<int64_t>(h) * o_head_stride;
+      for (int d = threadIdx.x; d < head_dim; d += blockDim.x) store_out<T>(out + d, NAN);
+      if (threadIdx.x == 0) lse[bh] = NAN;
+    }
+    // Every CTA has read n before the last one to count itself advances it.
+    if (threadIdx.x == 0) {
+      __threadfence();
+      if (atomicAdd(wait.merge_done, 1u) == gridDim.x - 1) {
+        *wait.merge_done = 0u;
+        *wait.step_word = n + 1;
+      }
+    }
     if (s_failed) return;
   }
   auto load = [](const float* p) { return kPeers ? __ldcg(p) : *p; };
-  const int bh = blockIdx.x;
-  const int b = bh / heads;
-  const int h = bh - b * heads;
   const int64_t base = static_cast<int64_t>(bh) * num_splits;
   float m = -INFINITY;
   for (int s = 0; s < num_splits; ++s) m = fmaxf(m, load(partial_ml + 2 * (base + s)));
@@ -1539,10 +1595,18 @@ struct ExchangeLayout {
   size_t region;        // one parity region
 };
 
+// Words of the counter block (uint64 each): [0, world) arrivals per source rank, then this
+// rank's CTA count of the push in progress, the CTA count of the merge in progress and its
+// completed-step count.
+constexpr int kPushCtasWord = 0, kMergeCtasWord = 1, kStepWord = 2;   // after the arrivals
+
+size_t counter_block_bytes(int world) {
+  return align256(static_cast<size_t>(world + 3) * sizeof(unsigned long long));
+}
+
 ExchangeLayout exchange_layout(int world, int batch, int heads, int head_dim, int splits) {
   ExchangeLayout l;
-  // world arrival counters, then this rank's CTA count of the current push.
-  l.counters = align256(static_cast<size_t>(world + 1) * sizeof(unsigned long long));
+  l.counters = counter_block_bytes(world);
   const size_t slots = static_cast<size_t>(batch) * heads * world * splits;
   l.po_bytes = align256(slots * head_dim * sizeof(float));
   l.region = align256(l.po_bytes + slots * 2 * sizeof(float));
@@ -1575,8 +1639,7 @@ extern "C" size_t flb_peer_exchange_bytes(int32_t world, int32_t batch, int32_t 
 
 extern "C" int flb_decode_partials_push(const flb_decode_params* p, int32_t key_begin,
                                         int32_t key_end, int32_t seq_offset,
-                                        const flb_peer_exchange* x, int32_t parity,
-                                        flb_stream_t stream_) {
+                                        const flb_peer_exchange* x, flb_stream_t stream_) {
   clear_error();
   if (p == nullptr) return fail(FLB_ERR_INVALID_ARGUMENT, "params is NULL");
   if (int st = check_exchange(x)) return st;
@@ -1588,7 +1651,6 @@ extern "C" int flb_decode_partials_push(const flb_decode_params* p, int32_t key_
   if (key_begin < 0 || key_end < key_begin)
     return fail(FLB_ERR_INVALID_ARGUMENT, "bad key window [%d, %d)", key_begin, key_end);
   if (q.num_splits < 1) return fail(FLB_ERR_INVALID_ARGUMENT, "num_splits must be >= 1 here");
-  if (parity != 0 && parity != 1) return fail(FLB_ERR_INVALID_ARGUMENT, "parity must be 0 or 1");
   if (q.block_tables != nullptr && key_begin % tile_keys_for(&q) != 0)
     return fail(FLB_ERR_UNSUPPORTED, "paged cache: key_begin %d must be a multiple of %d",
                 key_begin, tile_keys_for(&q));
@@ -1610,13 +1672,16 @@ extern "C" int flb_decode_partials_push(const flb_decode_params* p, int32_t key_
   const ExchangeLayout l = exchange_layout(x->world, q.batch, q.heads, q.head_dim, q.num_splits);
   a.n_dest = x->world;
   for (int r = 0; r < x->world; ++r) {
-    char* region = static_cast<char*>(x->buffers[r]) + l.counters + parity * l.region;
+    char* region = static_cast<char*>(x->buffers[r]) + l.counters;   // parity region 0
     a.partial_o[r] = reinterpret_cast<float*>(region);
     a.partial_ml[r] = reinterpret_cast<float*>(region + l.po_bytes);
     a.arrive[r] = static_cast<unsigned long long*>(x->buffers[r]) + x->rank;
   }
-  a.cta_done = reinterpret_cast<unsigned int*>(
-      static_cast<unsigned long long*>(x->buffers[x->rank]) + x->world);
+  unsigned long long* own = static_cast<unsigned long long*>(x->buffers[x->rank]);
+  a.cta_done = reinterpret_cast<unsigned int*>(own + x->world + kPushCtasWord);
+  a.step_word = own + x->world + kStepWord;
+  a.region_o = static_cast<int64_t>(l.region / sizeof(float));
+  a.region_ml = a.region_o;
   const int grid_y = q.batch * q.heads_kv * a.head_chunks;
   if (grid_y > 65535)
     return fail(FLB_ERR_UNSUPPORTED, "batch * heads_kv * head chunks = %d exceeds 65535", grid_y);
@@ -1625,8 +1690,7 @@ extern "C" int flb_decode_partials_push(const flb_decode_params* p, int32_t key_
                           deep_fits(q.num_splits, grid_y, sm_count));
 }
 
-extern "C" int flb_decode_merge_peers(const flb_peer_exchange* x, int32_t parity,
-                                      uint64_t expected, int32_t batch, int32_t heads,
+extern "C" int flb_decode_merge_peers(const flb_peer_exchange* x, int32_t batch, int32_t heads,
                                       int32_t head_dim, int32_t splits_per_rank, int32_t dtype,
                                       void* o, int64_t o_batch_stride, int64_t o_head_stride,
                                       float* lse, int32_t* status, flb_stream_t stream_) {
@@ -1635,20 +1699,31 @@ extern "C" int flb_decode_merge_peers(const flb_peer_exchange* x, int32_t parity
   if (!o || !lse) return fail(FLB_ERR_INVALID_ARGUMENT, "a required pointer is NULL");
   if (batch <= 0 || heads <= 0 || splits_per_rank <= 0 || (head_dim != 64 && head_dim != 128))
     return fail(FLB_ERR_INVALID_ARGUMENT, "bad merge shape");
-  if (parity != 0 && parity != 1) return fail(FLB_ERR_INVALID_ARGUMENT, "parity must be 0 or 1");
+  if (batch * heads > 0x7fffffff / 2) return fail(FLB_ERR_UNSUPPORTED, "merge grid too large");
   const ExchangeLayout l = exchange_layout(x->world, batch, heads, head_dim, splits_per_rank);
-  const char* region =
-      static_cast<const char*>(x->buffers[x->rank]) + l.counters + parity * l.region;
+  const char* region = static_cast<const char*>(x->buffers[x->rank]) + l.counters;
   const float* po = reinterpret_cast<const float*>(region);
   const float* pml = reinterpret_cast<const float*>(region + l.po_bytes);
+  unsigned long long* own = static_cast<unsigned long long*>(x->buffers[x->rank]);
   PeerWait wait;
-  wait.counters = static_cast<const unsigned long long*>(x->buffers[x->rank]);
+  wait.counters = own;
+  wait.step_word = own + x->world + kStepWord;
+  wait.merge_done = reinterpret_cast<unsigned int*>(own + x->world + kMergeCtasWord);
   wait.world = x->world;
-  wait.expected = expected;
+  wait.region_o = static_cast<int64_t>(l.region / sizeof(float));
+  wait.region_ml = wait.region_o;
   wait.timeout_ns = x->timeout_ns > 0 ? x->timeout_ns : static_cast<int64_t>(kWaitTimeoutNs);
   wait.status = status;
   const int splits = x->world * splits_per_rank;
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
   return launch_merge_any<true>(dtype, po, pml, batch, heads, head_dim, splits, o,
                                 o_batch_stride, o_head_stride, lse, stream, wait);
+}
+
+extern "C" int flb_peer_exchange_reset(const flb_peer_exchange* x, flb_stream_t stream_) {
+  clear_error();
+  if (int st = check_exchange(x)) return st;
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
+  return check_cuda(cudaMemsetAsync(x->buffers[x->rank], 0, counter_block_bytes(x->world), stream),
+                    "cudaMemsetAsync(exchange counters)");
 }

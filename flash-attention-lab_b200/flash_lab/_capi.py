@@ -96,9 +96,10 @@ SIGNATURES = {
     "flb_peer_free": ([_p], ctypes.c_int),
     "flb_peer_exchange_bytes": ([_i32, _i32, _i32, _i32, _i32], ctypes.c_size_t),
     "flb_decode_partials_push": ([ctypes.POINTER(DecodeParams), _i32, _i32, _i32,
-                                  ctypes.POINTER(PeerExchange), _i32, _p], ctypes.c_int),
-    "flb_decode_merge_peers": ([ctypes.POINTER(PeerExchange), _i32, ctypes.c_uint64, _i32, _i32,
-                                _i32, _i32, _i32, _p, _i64, _i64, _p, _p, _p], ctypes.c_int),
+                                  ctypes.POINTER(PeerExchange), _p], ctypes.c_int),
+    "flb_decode_merge_peers": ([ctypes.POINTER(PeerExchange), _i32, _i32, _i32, _i32, _i32, _p,
+                                _i64, _i64, _p, _p, _p], ctypes.c_int),
+    "flb_peer_exchange_reset": ([ctypes.POINTER(PeerExchange), _p], ctypes.c_int),
 }
 
 _LIB: ctypes.CDLL | None = None

@@ -22,11 +22,19 @@ There is no CPU path: the kernels are the library's, and only the collective is 
 
 With a PeerExchange, phases 1 and 2 are one kernel: each rank's split kernel stores its partials
 straight into every rank's exchange buffer over NVLink (CUDA IPC peer mappings); its last CTA to
-finish then adds one arrival to this rank's counter in every buffer (release, system scope). Phase 3 waits on the
-device, bounded by a timeout, until every source's counter has reached the step's expected count,
-and merges; no NCCL call is on the path. Buffers alternate by step parity, so a rank that runs one
-step ahead cannot overwrite partials another rank is still merging. The result is bitwise equal
-to the all-gather path (same partials, same merge order).
+finish then adds one arrival to this rank's counter in every buffer (release, system scope).
+Phase 3 waits on the device, bounded by a timeout, until every source's counter has reached the
+step's count, and merges; no NCCL call is on the path. Buffers alternate by step parity, so a rank
+that runs one step ahead cannot overwrite partials another rank is still merging. The step count
+lives in device memory (the merge advances it), so a decode step with an exchange can be captured
+in a CUDA graph and replayed. The result is bitwise equal to the all-gather path (same partials,
+same merge order).
+
+Prefill shards over (batch, KV head) units with no communication (attention_sharded): rank r of N
+takes units [r U / N, (r + 1) U / N) of the U = B * H_kv units in batch-major order, each unit a
+KV head with its query heads, as at most three rectangular views of q, k and v. Every row of the
+output depends only on its own (batch, head) inputs, so the shards' outputs are bitwise those of
+one unsharded call.
 
 No counterpart in the reference, which is single-GPU (README.md:183 there); the merge follows
 its split merge (csrc/decode/decode.cu:204-228).
@@ -137,13 +145,30 @@ def gather_in_rank_order(po: torch.Tensor, pml: torch.Tensor, group=None):
     return merged[..., :head_dim].contiguous(), merged[..., head_dim:].contiguous()
 
 
+class _DeviceWords:
+    """A non-owning view of n int64 words of device memory (the exchange's counter block), for
+    torch.as_tensor through the CUDA array interface."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<i8", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
 class PeerExchange:
     """Exchange buffers for decode_sharded over peer memory, one per (process group, shape).
 
     Collective: every rank of `group` constructs it with the same shapes, with its own GPU
     current. Each rank allocates one buffer (flb_peer_alloc), the CUDA IPC handles are
-    all-gathered over the process group once, and every rank maps the others' buffers. Not for
-    CUDA-graph capture: the expected arrival count is a host value that grows with every step.
+    all-gathered over the process group once, and every rank maps the others' buffers.
+
+    The step count, which selects the parity region and the arrival count to wait for, is kept
+    in this rank's buffer on the device, so decode_sharded(..., exchange=...) can be captured in
+    a CUDA graph; every replay is one step.
+
+    Failure is sticky. When a wait times out (a rank did not push in time), `status` gets code 2
+    and that step's o and lse are NaN; from then on this rank's pushes publish nothing and its
+    merges return NaN at once, so the other ranks fail the same way rather than merging stale
+    partials. reset() (collective) clears the failure.
     """
 
     def __init__(self, batch: int, heads: int, head_dim: int, splits_per_rank: int = 1,
@@ -187,22 +212,40 @@ class PeerExchange:
             x.buffers[r] = ptr.value
             self._opened.append(ptr.value)
         self.x = x
-        self.steps = 0       # decode steps taken (selects the parity region)
-        self.expected = 0    # arrivals every source counter has reached after those steps
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        # This rank's counter block: arrivals per source, push and merge CTA counts, step count.
+        self._words = torch.as_tensor(_DeviceWords(self._own, self.world + 3), device=self.device)
 
     def read_status(self) -> int:
         """Device status of the exchange waits (0, or 2 when a peer's partials timed out);
-        synchronises and clears it."""
-        code = int(self.status.item())
+        synchronises. The code stays set (the exchange stays failed) until reset()."""
+        return int(self.status.item())
+
+    def steps(self) -> int:
+        """Decode steps this rank has merged (read from the device; synchronises)."""
+        return int(self._words[self.world + 2].item())
+
+    def reset(self) -> None:
+        """Collective: clears a failure. Every rank waits for its own work, then all zero their
+        counters and status words together, so the next step starts from step 0 everywhere."""
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)   # no rank still pushes into another's counters
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        rc = self._lib.flb_peer_exchange_reset(ctypes.byref(self.x), stream)
+        if rc != _capi.FLB_OK:
+            raise RuntimeError(f"flb_peer_exchange_reset: {_capi.error_message(self._lib, rc)}")
         self.status.zero_()
-        return code
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
 
     def close(self) -> None:
         """Collective: unmaps the peers' buffers and frees this rank's buffer."""
         if self._own is None:
             return
         torch.cuda.synchronize(self.device)
+        self._words = None
         if self.world > 1:
             dist.barrier(group=self.group)      # nobody still writes into a buffer being freed
         for ptr in self._opened:
@@ -231,16 +274,13 @@ def _decode_sharded_peer(q3, k_shard, v_shard, seq_lens, seq_offset, splits, sca
         batch, heads, k_shard.shape[2], head_dim, k_shard.shape[1], splits, _dtype_code(q3.dtype),
         float(scale), 0, 0, exchange.status.data_ptr(),
     )
-    parity = exchange.steps & 1
     rc = lib.flb_decode_partials_push(ctypes.byref(p), 0, k_shard.shape[1], int(seq_offset),
-                                      ctypes.byref(exchange.x), parity, stream)
+                                      ctypes.byref(exchange.x), stream)
     if rc != _capi.FLB_OK:
         raise RuntimeError(f"flb_decode_partials_push: {_capi.error_message(lib, rc)}")
-    exchange.expected += 1
-    exchange.steps += 1
     o = torch.empty((batch, heads, head_dim), device=q3.device, dtype=q3.dtype)
     lse = torch.empty((batch, heads), device=q3.device, dtype=torch.float32)
-    rc = lib.flb_decode_merge_peers(ctypes.byref(exchange.x), parity, exchange.expected, batch,
+    rc = lib.flb_decode_merge_peers(ctypes.byref(exchange.x), batch,
                                     heads, head_dim, splits, _dtype_code(q3.dtype), o.data_ptr(),
                                     o.stride(0), o.stride(1), lse.data_ptr(),
                                     exchange.status.data_ptr(), stream)
@@ -260,8 +300,10 @@ def decode_sharded(q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.Tensor
     [B, S_shard, H_kv, D] hold keys [shard.offset, shard.offset + shard.length) of every
     sequence; seq_lens [B] int32 are the global lengths. Returns o (q's shape) and, with
     return_lse, the natural-log LSE [B, H], on every rank. With `exchange`, the partials move
-    over peer memory (one fused push kernel per rank) instead of an all_gather; a wait that
-    times out leaves code 2 in exchange.status (exchange.read_status()).
+    over peer memory (one fused push kernel per rank) instead of an all_gather, with no host
+    synchronisation and no host-side step state (the call can be captured in a CUDA graph); a
+    wait that times out leaves code 2 in exchange.status and NaN in o and lse, and the exchange
+    stays failed until exchange.reset().
     """
     if splits_per_rank < 1:
         raise ValueError(f"splits_per_rank must be positive, got {splits_per_rank}")
@@ -285,3 +327,137 @@ def decode_sharded(q: torch.Tensor, k_shard: torch.Tensor, v_shard: torch.Tensor
     if q.dim() == 4:
         o = o.unsqueeze(1)
     return (o, lse) if return_lse else o
+
+
+# ------------------------------------------------------------------------------------------------
+# Prefill sharded over (batch, KV head) units
+# ------------------------------------------------------------------------------------------------
+
+@dataclass(frozen=True)
+class PrefillPiece:
+    """Batches [b0, b1) x KV heads [g0, g1) (with their query heads) of one prefill problem."""
+
+    b0: int
+    b1: int
+    g0: int
+    g1: int
+
+    @property
+    def units(self) -> int:
+        return (self.b1 - self.b0) * (self.g1 - self.g0)
+
+
+def prefill_pieces(batch: int, heads_kv: int, world_size: int, rank: int) -> list[PrefillPiece]:
+    """The units [rank U / N, (rank + 1) U / N) of the U = batch * heads_kv (batch, KV head)
+    units, batch-major, as rectangles: the tail of a first batch, whole batches, the head of a
+    last batch (at most three pieces). A function of shapes only, the same on every rank."""
+    if world_size < 1 or not 0 <= rank < world_size:
+        raise ValueError(f"rank {rank} of world {world_size}")
+    units = batch * heads_kv
+    u, u1 = rank * units // world_size, (rank + 1) * units // world_size
+    pieces = []
+    while u < u1:
+        b, g = divmod(u, heads_kv)
+        if g == 0 and u1 - u >= heads_kv:
+            nb = (u1 - u) // heads_kv
+            pieces.append(PrefillPiece(b, b + nb, 0, heads_kv))
+            u += nb * heads_kv
+        else:
+            g1 = min(heads_kv, g + (u1 - u))
+            pieces.append(PrefillPiece(b, b + 1, g, g1))
+            u += g1 - g
+    return pieces
+
+
+@dataclass
+class ShardedPrefill:
+    """This rank's part of a sharded prefill: per piece, o [b1-b0, S_q, (g1-g0) group, D] and lse
+    [b1-b0, (g1-g0) group, S_q] (fp32)."""
+
+    shape: tuple          # (B, S_q, H, H_kv, D) of the whole problem
+    world_size: int
+    rank: int
+    pieces: list
+    outputs: list         # [(o, lse)] per piece
+
+    def gather(self, group=None):
+        """Collective: the whole o [B, S_q, H, D] and lse [B, H, S_q] on every rank (one padded
+        all_gather each for o and lse). Outside the sharded step: the step itself exchanges
+        nothing."""
+        batch, seqlen_q, heads, heads_kv, head_dim = self.shape
+        grp = heads // heads_kv
+        o0 = self.outputs[0][0] if self.outputs else None
+        device = o0.device if o0 is not None else torch.device("cuda", torch.cuda.current_device())
+        dtype = o0.dtype if o0 is not None else torch.bfloat16
+        ldtype = self.outputs[0][1].dtype if self.outputs else torch.float32
+        per_unit_o = seqlen_q * grp * head_dim
+        per_unit_l = grp * seqlen_q
+        cap = -(-batch * heads_kv // self.world_size)     # most units any rank holds
+        flat_o = torch.zeros(cap * per_unit_o, device=device, dtype=dtype)
+        flat_l = torch.zeros(cap * per_unit_l, device=device, dtype=ldtype)
+        at = 0
+        for piece, (o, lse) in zip(self.pieces, self.outputs):
+            n = piece.units
+            # units in (b, g) order: o [nb, S, ng*grp, D] -> [nb, ng, S, grp, D]
+            ob = o.view(piece.b1 - piece.b0, seqlen_q, piece.g1 - piece.g0, grp, head_dim)
+            flat_o[at * per_unit_o:(at + n) * per_unit_o].copy_(ob.transpose(1, 2).reshape(-1))
+            flat_l[at * per_unit_l:(at + n) * per_unit_l].copy_(lse.reshape(-1))
+            at += n
+        if self.world_size > 1:
+            all_o = torch.empty(self.world_size * flat_o.numel(), device=device, dtype=dtype)
+            all_l = torch.empty(self.world_size * flat_l.numel(), device=device, dtype=ldtype)
+            dist.all_gather_into_tensor(all_o, flat_o, group=group)
+            dist.all_gather_into_tensor(all_l, flat_l, group=group)
+        else:
+            all_o, all_l = flat_o, flat_l
+        out = torch.empty((batch, seqlen_q, heads, head_dim), device=device, dtype=dtype)
+        lse_all = torch.empty((batch, heads, seqlen_q), device=device, dtype=ldtype)
+        for r in range(self.world_size):
+            at = 0
+            for piece in prefill_pieces(batch, heads_kv, self.world_size, r):
+                n = piece.units
+                nb, ng = piece.b1 - piece.b0, piece.g1 - piece.g0
+                src_o = all_o[(r * cap + at) * per_unit_o:(r * cap + at + n) * per_unit_o]
+                src_l = all_l[(r * cap + at) * per_unit_l:(r * cap + at + n) * per_unit_l]
+                h0, h1 = piece.g0 * grp, piece.g1 * grp
+                out[piece.b0:piece.b1, :, h0:h1].copy_(
+                    src_o.view(nb, ng, seqlen_q, grp, head_dim).transpose(1, 2)
+                    .reshape(nb, seqlen_q, ng * grp, head_dim))
+                lse_all[piece.b0:piece.b1, h0:h1].copy_(src_l.view(nb, ng * grp, seqlen_q))
+                at += n
+        return out, lse_all
+
+
+def attention_sharded(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = False,
+                      softmax_scale: float | None = None, group=None,
+                      world_size: int | None = None, rank: int | None = None) -> ShardedPrefill:
+    """This rank's share of flash_lab.attention(q, k, v) over the ranks of `group`.
+
+    q [B, S_q, H, D], k / v [B, S_k, H_kv, D] are the whole problem (the same on every rank; only
+    the views of this rank's pieces are read). Rank r computes the (batch, KV head) units
+    prefill_pieces(B, H_kv, N, r) with one flash_lab.attention call per piece on zero-copy head /
+    batch slices. No communication; ShardedPrefill.gather() assembles the whole output when a
+    caller needs it. world_size / rank default to the process group's.
+    """
+    from flash_lab import ops
+
+    if world_size is None:
+        multi = dist.is_initialized()
+        world_size = dist.get_world_size(group) if multi else 1
+        rank = dist.get_rank(group) if multi else 0
+    elif rank is None:
+        raise ValueError("rank is required with world_size")
+    batch, seqlen_q, heads, head_dim = q.shape
+    heads_kv = k.shape[2]
+    if heads % heads_kv != 0:
+        raise ValueError(f"heads {heads} must be a multiple of heads_kv {heads_kv}")
+    grp = heads // heads_kv
+    pieces = prefill_pieces(batch, heads_kv, world_size, rank)
+    outputs = []
+    for pc in pieces:
+        h0, h1 = pc.g0 * grp, pc.g1 * grp
+        outputs.append(ops.attention(q[pc.b0:pc.b1, :, h0:h1], k[pc.b0:pc.b1, :, pc.g0:pc.g1],
+                                     v[pc.b0:pc.b1, :, pc.g0:pc.g1], causal=causal,
+                                     softmax_scale=softmax_scale, return_lse=True))
+    return ShardedPrefill((batch, seqlen_q, heads, heads_kv, head_dim), world_size, rank, pieces,
+                          outputs)

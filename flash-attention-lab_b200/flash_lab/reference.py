@@ -69,6 +69,51 @@ def attention_rows(q, k, v, rows: torch.Tensor, causal: bool = False, softmax_sc
     return out
 
 
+def attention_tiled(q, k, v, causal: bool = False, softmax_scale=None, return_lse: bool = False,
+                    block_q: int = 64, block_k: int = 64, dtype: torch.dtype = torch.float64):
+    """attention() computed block by block with the online softmax, never forming the full
+    [S_q, S_k] score matrix (the reference's reference.py:90-152). Blocks wholly above the
+    causal diagonal are skipped and blocks crossing it are masked; while a row has seen only
+    masked keys its reference point is 0, so its exponentials are exactly 0. Returns o
+    [B, S_q, H, D] in `dtype` (and lse [B, H, S_q])."""
+    shape = check_attention_inputs(q, k, v, require_unit_stride=False)
+    scale = _scale(shape.head_dim, softmax_scale)
+    offset = shape.seqlen_k - shape.seqlen_q
+    qh = q.to(dtype).transpose(1, 2)                        # [B, H, S_q, D]
+    kh = _kv(k, shape.group, dtype).transpose(1, 2)         # [B, H, S_k, D]
+    vh = _kv(v, shape.group, dtype).transpose(1, 2)
+    out = torch.zeros_like(qh)
+    lse = torch.full(qh.shape[:-1], float("-inf"), dtype=dtype, device=q.device)
+    for q0 in range(0, shape.seqlen_q, block_q):
+        q1 = min(q0 + block_q, shape.seqlen_q)
+        m = torch.full((shape.batch, shape.heads, q1 - q0), float("-inf"), dtype=dtype,
+                       device=q.device)
+        l = torch.zeros_like(m)
+        acc = torch.zeros((*m.shape, shape.head_dim), dtype=dtype, device=q.device)
+        stop = min(shape.seqlen_k, q1 + offset) if causal else shape.seqlen_k
+        for k0 in range(0, max(stop, 0), block_k):
+            k1 = min(k0 + block_k, shape.seqlen_k)
+            s = qh[:, :, q0:q1] @ kh[:, :, k0:k1].transpose(-1, -2) * scale
+            if causal and k1 - 1 > q0 + offset:
+                hidden = (torch.arange(k0, k1, device=q.device)[None, :]
+                          > torch.arange(q0, q1, device=q.device)[:, None] + offset)
+                s = s.masked_fill(hidden, float("-inf"))
+            m_new = torch.maximum(m, s.amax(dim=-1))
+            ref = torch.where(torch.isneginf(m_new), torch.zeros_like(m_new), m_new)
+            alpha = torch.exp(m - ref)
+            p = torch.exp(s - ref[..., None])
+            l = alpha * l + p.sum(dim=-1)
+            acc = alpha[..., None] * acc + p @ vh[:, :, k0:k1]
+            m = m_new
+        seen = l > 0
+        denom = torch.where(seen, l, torch.ones_like(l))
+        out[:, :, q0:q1] = acc / denom[..., None]
+        lse[:, :, q0:q1] = torch.where(seen, m + torch.log(denom),
+                                       torch.full_like(m, float("-inf")))
+    out = out.transpose(1, 2)
+    return (out, lse) if return_lse else out
+
+
 def gather_cache(cache: torch.Tensor, block_tables, batch_idx: int, length: int) -> torch.Tensor:
     """Rows 0..length-1 of one sequence as [length, H_kv, D], contiguous or paged cache."""
     if block_tables is None:

@@ -16,6 +16,9 @@
  *  - Every entry point returns an flb_status. Nothing throws or aborts across the ABI.
  *    flb_last_error() gives a message for the calling thread's most recent failure.
  *  - Reentrant: no mutable global state except one-time per-device kernel attribute set-up.
+ *    That set-up (shared-memory opt-ins, the static scratch address) is cached per device for
+ *    the life of the process, so the library must not be used on a device again after
+ *    cudaDeviceReset there.
  *  - Optional `status` device word: kernels whose pipeline waits exceed their deadline write a
  *    nonzero code there (first writer wins) and return early instead of hanging. Pass NULL to
  *    skip.
@@ -30,7 +33,7 @@
 extern "C" {
 #endif
 
-#define FLB_ABI_VERSION 2
+#define FLB_ABI_VERSION 3
 
 /* Most ranks a peer exchange (cross-GPU decode merge over NVLink) connects. */
 #define FLB_MAX_PEERS 8
@@ -209,12 +212,18 @@ int flb_decode_merge(const float* partial_o, const float* partial_ml, int32_t ba
  * Each rank allocates one exchange buffer with flb_peer_alloc, sends the handle to the other
  * ranks (any host channel) and maps theirs with flb_peer_open. Buffer layout, for `world` ranks,
  * B sequences, H query heads, head_dim D and S splits per rank (W*S splits in global order):
- *   [0, 256 * ceil(8 (W + 1) / 256))  uint64 arrival counters, one per source rank, then the
- *                                    CTA count of this rank's push in progress (all start at 0)
+ *   [0, 256 * ceil(8 (W + 3) / 256))  uint64 words, all starting at 0: one arrival counter per
+ *                                    source rank, then the CTA counts of this rank's push and
+ *                                    merge in progress, then n, the steps this rank has merged
  *   then two parity regions, each partial_o [B, H, W*S, D] fp32 (256-byte aligned) followed by
  *   partial_ml [B, H, W*S, 2] fp32 (the flb_decode_partials layout).
- * Step n of a decode uses parity n % 2, so a rank one step ahead never overwrites partials a
- * slower rank is still merging.
+ * Step n (counted on the device) uses parity n % 2, so a rank one step ahead never overwrites
+ * partials a slower rank is still merging. Nothing on the host counts steps, so a push + merge
+ * pair can be captured in a CUDA graph and replayed.
+ * Failure is sticky: once the status word a push or merge is given is nonzero (a wait that timed
+ * out), pushes publish nothing and merges write NaN to o and lse without waiting, on this rank
+ * and, through their own timeouts, on the others, until every rank has called
+ * flb_peer_exchange_reset with no step in flight and cleared its status word.
  */
 size_t flb_peer_handle_bytes(void);
 /* cudaMalloc + zero-fill + CUDA IPC export of `bytes` of device memory on the current device. */
@@ -238,26 +247,29 @@ size_t flb_peer_exchange_bytes(int32_t world, int32_t batch, int32_t heads, int3
 /*
  * This rank's split stage (flb_decode_partials on keys [key_begin, key_end), seq_offset, with
  * params->num_splits splits) writing its partials at global split indices
- * [rank * S, rank * S + S) of parity region `parity` in EVERY rank's buffer. Once all its CTAs
- * have written, the launch adds 1, with release semantics at system scope, to counter [rank] of
- * every buffer: after n pushes every counter a rank waits on reads n.
+ * [rank * S, rank * S + S) of parity region n % 2 (n: this rank's step count) in EVERY rank's
+ * buffer. Once all its CTAs have written, the launch adds 1, with release semantics at system
+ * scope, to counter [rank] of every buffer: after n pushes every counter a rank waits on reads
+ * n. params->status is the exchange's status word (see the failure rule above).
  */
 int flb_decode_partials_push(const flb_decode_params* params, int32_t key_begin,
                              int32_t key_end, int32_t seq_offset,
-                             const flb_peer_exchange* exchange, int32_t parity,
-                             flb_stream_t stream);
+                             const flb_peer_exchange* exchange, flb_stream_t stream);
 
 /*
- * Waits until every source counter of this rank's buffer has reached `expected` (bounded by
- * exchange->timeout_ns; on expiry it writes code 2 to `status` and leaves o / lse unwritten),
- * then merges the W*S partials of parity region `parity` in global split order, exactly as
- * flb_decode_merge does.
+ * Step n of this rank: waits until every source counter of this rank's buffer has reached n + 1
+ * (bounded by exchange->timeout_ns; on expiry it writes code 2 to `status`, and o / lse get NaN),
+ * merges the W*S partials of parity region n % 2 in global split order, exactly as
+ * flb_decode_merge does, and advances n.
  */
-int flb_decode_merge_peers(const flb_peer_exchange* exchange, int32_t parity, uint64_t expected,
-                           int32_t batch, int32_t heads, int32_t head_dim,
-                           int32_t splits_per_rank, int32_t dtype, void* o,
+int flb_decode_merge_peers(const flb_peer_exchange* exchange, int32_t batch, int32_t heads,
+                           int32_t head_dim, int32_t splits_per_rank, int32_t dtype, void* o,
                            int64_t o_batch_stride, int64_t o_head_stride, float* lse,
                            int32_t* status, flb_stream_t stream);
+
+/* Zeroes this rank's counter block (arrivals, CTA counts, step count) on `stream`. Collective in
+ * effect: every rank resets, with no push or merge of any rank in flight, before the next step. */
+int flb_peer_exchange_reset(const flb_peer_exchange* exchange, flb_stream_t stream);
 
 /*
  * Unit test of the tcgen05 building blocks the prefill kernel uses (no reference counterpart;

@@ -39,7 +39,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_version_and_status_strings(lib):
-    assert lib.flb_version() == 2
+    assert lib.flb_version() == 3
     assert lib.flb_status_string(0) == b"ok"
     assert lib.flb_status_string(3) == b"misaligned pointer or stride"
     assert lib.flb_status_string(99) == b"unknown status"
@@ -111,11 +111,12 @@ def test_peer_exchange_host_validation(lib):
     p = _capi.DecodeParams()
     x = _capi.PeerExchange()
     x.world, x.rank = 2, 0           # buffers left NULL
-    assert lib.flb_decode_partials_push(ctypes.byref(p), 0, 1, 0, ctypes.byref(x), 0, None) \
+    assert lib.flb_decode_partials_push(ctypes.byref(p), 0, 1, 0, ctypes.byref(x), None) \
         == _capi.FLB_ERR_INVALID_ARGUMENT
     assert b"buffer of rank 0" in lib.flb_last_error()
+    assert lib.flb_peer_exchange_reset(ctypes.byref(x), None) == _capi.FLB_ERR_INVALID_ARGUMENT
     x.world = 9
-    assert lib.flb_decode_merge_peers(ctypes.byref(x), 0, 1, 1, 32, 128, 1, 0, None, 0, 0, None,
+    assert lib.flb_decode_merge_peers(ctypes.byref(x), 1, 32, 128, 1, 0, None, 0, 0, None,
                                       None, None) == _capi.FLB_ERR_INVALID_ARGUMENT
     assert lib.flb_peer_alloc(0, ctypes.byref(ctypes.c_void_p()), None) \
         == _capi.FLB_ERR_INVALID_ARGUMENT

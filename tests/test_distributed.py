@@ -21,10 +21,13 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
+import flash_lab
 import oracle
 from flash_lab import _capi
-from flash_lab.distributed import (ShardSpec, decode_sharded, default_splits_per_rank,
-                                   local_lengths, merge_partials)
+from flash_lab import reference
+from flash_lab.distributed import (ShardedPrefill, ShardSpec, decode_sharded,
+                                   default_splits_per_rank, local_lengths, merge_partials,
+                                   prefill_pieces)
 
 TILE = 64  # keys per decode tile: split ranges are whole numbers of tiles
 
@@ -229,6 +232,93 @@ def test_two_gpus_over_nccl():
         assert p.exitcode == 0
 
 
+@pytest.mark.parametrize("batch,heads_kv,world", [(4, 32, 1), (4, 32, 2), (4, 32, 8),
+                                                   (4, 32, 3), (3, 5, 7), (2, 8, 16), (1, 1, 2)])
+def test_prefill_pieces_cover_every_unit_once(batch, heads_kv, world):
+    seen = {}
+    for rank in range(world):
+        pieces = prefill_pieces(batch, heads_kv, world, rank)
+        assert len(pieces) <= 3
+        assert sum(p.units for p in pieces) == \
+            (rank + 1) * batch * heads_kv // world - rank * batch * heads_kv // world
+        for p in pieces:
+            for b in range(p.b0, p.b1):
+                for g in range(p.g0, p.g1):
+                    seen[(b, g)] = seen.get((b, g), 0) + 1
+    assert seen == {(b, g): 1 for b in range(batch) for g in range(heads_kv)}
+
+
+def _sharded_prefill_rank(rank, world, port, results):
+    # Each rank computes its pieces with the fp64 torch reference (no GPU) and the gather puts
+    # the whole output together on every rank.
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        gen = torch.Generator().manual_seed(3)
+        batch, seqlen, heads, heads_kv, d = 3, 20, 6, 3, 16
+        q = torch.randn(batch, seqlen, heads, d, generator=gen, dtype=torch.float64)
+        k = torch.randn(batch, seqlen, heads_kv, d, generator=gen, dtype=torch.float64)
+        v = torch.randn(batch, seqlen, heads_kv, d, generator=gen, dtype=torch.float64)
+        grp = heads // heads_kv
+        pieces = prefill_pieces(batch, heads_kv, world, rank)
+        outs = []
+        for pc in pieces:
+            h0, h1 = pc.g0 * grp, pc.g1 * grp
+            outs.append(reference.attention(q[pc.b0:pc.b1, :, h0:h1], k[pc.b0:pc.b1, :, pc.g0:pc.g1],
+                                            v[pc.b0:pc.b1, :, pc.g0:pc.g1], causal=True,
+                                            return_lse=True))
+        sp = ShardedPrefill((batch, seqlen, heads, heads_kv, d), world, rank, pieces, outs)
+        o, lse = sp.gather()
+        o_ref, lse_ref = reference.attention(q, k, v, causal=True, return_lse=True)
+        results[rank] = bool(torch.allclose(o, o_ref, rtol=0, atol=1e-12)
+                             and torch.allclose(lse, lse_ref, rtol=0, atol=1e-12))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_prefill_gather_on_two_gloo_ranks():
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as manager:
+        results = manager.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_sharded_prefill_rank, args=(r, 2, port, results))
+                 for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=120)
+            assert p.exitcode == 0
+        assert dict(results) == {0: True, 1: True}
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [3, 8])
+def test_attention_sharded_pieces_equal_the_unsharded_call(world):
+    # Emulated ranks on one GPU: every piece of every rank is bitwise the matching slice of one
+    # unsharded call (rows depend only on their own (batch, head) inputs).
+    from flash_lab.distributed import attention_sharded
+
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    batch, seqlen, heads, heads_kv, d = 3, 600, 8, 4, 128
+    q = torch.randn(batch, seqlen, heads, d, device="cuda", dtype=torch.bfloat16, generator=gen)
+    k = torch.randn(batch, seqlen, heads_kv, d, device="cuda", dtype=torch.bfloat16, generator=gen)
+    v = torch.randn(batch, seqlen, heads_kv, d, device="cuda", dtype=torch.bfloat16, generator=gen)
+    for causal in (False, True):
+        o_full, lse_full = flash_lab.attention(q, k, v, causal=causal, return_lse=True)
+        covered = 0
+        for rank in range(world):
+            sp = attention_sharded(q, k, v, causal=causal, world_size=world, rank=rank)
+            for pc, (o, lse) in zip(sp.pieces, sp.outputs):
+                h0, h1 = pc.g0 * 2, pc.g1 * 2
+                assert torch.equal(o, o_full[pc.b0:pc.b1, :, h0:h1]), (rank, pc)
+                assert torch.equal(lse, lse_full[pc.b0:pc.b1, h0:h1]), (rank, pc)
+                covered += pc.units
+        assert covered == batch * heads_kv
+    sp = attention_sharded(q, k, v, causal=True, world_size=1, rank=0)
+    o, lse = sp.gather()
+    assert torch.equal(o, o_full) and torch.equal(lse, lse_full)
+
+
 @pytest.mark.gpu
 def test_peer_exchange_single_rank_matches_all_gather_path():
     # World of one: the push kernel writes into this rank's own exchange buffer and the merge
@@ -251,7 +341,45 @@ def test_peer_exchange_single_rank_matches_all_gather_path():
                                     return_lse=True, exchange=ex)
             assert torch.equal(o, o_ref) and torch.equal(lse, lse_ref), step
         assert ex.read_status() == 0
-        assert ex.steps == 3
+        assert ex.steps() == 3
+    finally:
+        ex.close()
+
+
+@pytest.mark.gpu
+def test_peer_exchange_step_replays_from_a_cuda_graph():
+    # The step count lives on the device, so a captured push + merge replays as successive
+    # steps (alternating parity regions); each replay equals the all-gather path bitwise.
+    from flash_lab.distributed import PeerExchange
+
+    gen = torch.Generator(device="cuda").manual_seed(12)
+    batch, heads, heads_kv, smax, d, splits = 2, 16, 4, 2048, 128, 2
+    kc = torch.randn(batch, smax, heads_kv, d, device="cuda", dtype=torch.bfloat16, generator=gen)
+    vc = torch.randn(batch, smax, heads_kv, d, device="cuda", dtype=torch.bfloat16, generator=gen)
+    lens = torch.tensor([2000, 700], device="cuda", dtype=torch.int32)
+    q = torch.randn(batch, heads, d, device="cuda", dtype=torch.bfloat16, generator=gen)
+    shard = ShardSpec(0, smax)
+    ex = PeerExchange(batch, heads, d, splits_per_rank=splits)
+    try:
+        decode_sharded(q, kc, vc, lens, shard, splits_per_rank=splits, exchange=ex)  # warm-up
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            o_g, lse_g = decode_sharded(q, kc, vc, lens, shard, splits_per_rank=splits,
+                                        return_lse=True, exchange=ex)
+        for step in range(4):
+            q.copy_(torch.randn(batch, heads, d, device="cuda", dtype=torch.bfloat16,
+                                generator=gen))
+            lens.copy_(torch.tensor([2048 - 300 * step, 1 + 200 * step], device="cuda",
+                                    dtype=torch.int32))
+            graph.replay()
+            o_ref, lse_ref = decode_sharded(q, kc, vc, lens, shard, splits_per_rank=splits,
+                                            return_lse=True)
+            torch.cuda.synchronize()
+            assert torch.equal(o_g, o_ref) and torch.equal(lse_g, lse_ref), step
+        assert ex.read_status() == 0
+        assert ex.steps() == 5          # the warm-up and four replays (capture runs nothing)
+        del graph
     finally:
         ex.close()
 
@@ -265,18 +393,39 @@ def test_peer_exchange_wait_times_out_with_a_status():
     ex = PeerExchange(1, 8, 64, splits_per_rank=1, timeout_s=0.02)
     try:
         lib = _capi.load()
-        o = torch.zeros(1, 8, 64, device="cuda", dtype=torch.bfloat16)
-        lse = torch.zeros(1, 8, device="cuda")
-        rc = lib.flb_decode_merge_peers(ctypes.byref(ex.x), 0, 1, 1, 8, 64, 1, _capi.FLB_BF16,
-                                        o.data_ptr(), o.stride(0), o.stride(1), lse.data_ptr(),
-                                        ex.status.data_ptr(),
-                                        torch.cuda.current_stream().cuda_stream)
-        assert rc == 0
+
+        def merge_only():
+            o = torch.zeros(1, 8, 64, device="cuda", dtype=torch.bfloat16)
+            lse = torch.zeros(1, 8, device="cuda")
+            rc = lib.flb_decode_merge_peers(ctypes.byref(ex.x), 1, 8, 64, 1, _capi.FLB_BF16,
+                                            o.data_ptr(), o.stride(0), o.stride(1),
+                                            lse.data_ptr(), ex.status.data_ptr(),
+                                            torch.cuda.current_stream().cuda_stream)
+            assert rc == 0
+            torch.cuda.synchronize()
+            return o, lse
+
+        o, lse = merge_only()                   # no push came: the wait times out
         assert ex.read_status() == 2
-        assert not o.any()                      # nothing merged
+        assert torch.isnan(o).all() and torch.isnan(lse).all()
+        # Sticky: the next merge fails at once (no second timeout) and the status stays.
+        o, lse = merge_only()
+        assert torch.isnan(o).all() and ex.read_status() == 2
+
         q = torch.randn(1, 1, 8, 64, device="cuda", dtype=torch.bfloat16)
         kc = torch.randn(1, 128, 8, 64, device="cuda", dtype=torch.bfloat16)
         lens = torch.tensor([100], device="cuda", dtype=torch.int32)
+        # A push on a failed exchange publishes nothing: its merge fails too.
+        o = decode_sharded(q, kc, kc, lens, ShardSpec(0, 128), exchange=ex)
+        torch.cuda.synchronize()
+        assert torch.isnan(o).all() and ex.read_status() == 2
+
+        ex.reset()                               # clears the failure: steps work again
+        assert ex.read_status() == 0 and ex.steps() == 0
+        o = decode_sharded(q, kc, kc, lens, ShardSpec(0, 128), exchange=ex)
+        o_ref = decode_sharded(q, kc, kc, lens, ShardSpec(0, 128))
+        torch.cuda.synchronize()
+        assert torch.equal(o, o_ref) and ex.read_status() == 0 and ex.steps() == 1
         import flash_lab
 
         flash_lab.decode(q, kc, kc, lens)       # the context still works
@@ -315,6 +464,24 @@ def _peer_rank(rank, world, port, seed):
             torch.cuda.synchronize()
             assert torch.equal(o, o_ref) and torch.equal(lse, lse_ref), (rank, step)
         assert ex.read_status() == 0
+        # The same step captured in a CUDA graph on both ranks and replayed: each replay is one
+        # exchange step, bitwise equal to the all-gather path.
+        qg = q.clone()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            o_g, lse_g = decode_sharded(qg, ks, vs, lens, shard, splits_per_rank=splits,
+                                        return_lse=True, exchange=ex)
+        for step in range(3):
+            qg.copy_(torch.randn(2, heads, d, device="cuda", dtype=torch.bfloat16,
+                                 generator=gen))
+            graph.replay()
+            o_ref, lse_ref = decode_sharded(qg, ks, vs, lens, shard, splits_per_rank=splits,
+                                            return_lse=True)
+            torch.cuda.synchronize()
+            assert torch.equal(o_g, o_ref) and torch.equal(lse_g, lse_ref), (rank, "graph", step)
+        assert ex.read_status() == 0 and ex.steps() == 7
+        del graph
+        q = qg
         ref = oracle.decode(q.double().cpu().numpy(), kc.double().cpu().numpy(),
                             vc.double().cpu().numpy(), lens.cpu().numpy())
         err = np.abs(o.double().cpu().numpy() - ref).max()
