@@ -69,14 +69,35 @@ struct Geometry {
   static constexpr int kSmemData = (kQTiles + kSlots) * kTileBytes;
   static constexpr int kSmemBytes = kSmemData + 1024 + 256;
 };
-// Warps: softmax WG0 (0-3), WG1 (4-7), producer (8), MMA issuer (9).
-constexpr int kThreads = 320;
+// Warps: softmax WG0 (0-3), WG1 (4-7), then WG2: producer (8), MMA issuer (9) and two warps with
+// no role (10, 11), which make WG2 a whole warpgroup for the register split: the launch gives
+// every thread 168 registers (384 x 168 = 64512 of the SM's 65536); WG2 then drops to
+// kControl and the softmax warpgroups rise to kSoftmax (2 x 128 x 216 + 128 x 72 = 64512). The
+// persistent form's control warps keep more state (item walk, per-buffer counts), so its split
+// is 208 / 88; each is the split with the fewest spills in ptxas's report.
+constexpr int kThreads = 384;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
+constexpr int kLaunchRegs = 168;
+template <bool kPersistent>
+struct RegSplit {
+  static constexpr int kSoftmax = kPersistent ? 208 : 216;
+  static constexpr int kControl = kPersistent ? 88 : 72;
+  static_assert(2 * 128 * kSoftmax + 128 * kControl <= kThreads * kLaunchRegs,
+                "the register split must fit in the launch's registers");
+};
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units: p <= 2^8 between rescales
 constexpr int kDefaultPolyPairs = 2;           // of every 8 score pairs, 2^x on the FMA pipe
-constexpr int kDefaultPChunks = 1;             // P published to the MMA warp in this many chunks
+#ifndef FLB_PREFILL_PERSISTENT_D128
+#define FLB_PREFILL_PERSISTENT_D128 0   // head_dim 128 with persistent CTAs (measurement knob)
+#endif
+#ifndef FLB_PREFILL_P_CHUNKS
+#define FLB_PREFILL_P_CHUNKS 1
+#endif
+constexpr int kDefaultPChunks = FLB_PREFILL_P_CHUNKS;   // P published to the MMA warp in this
+                                                        // many chunks (1 or 2)
+static_assert(kDefaultPChunks == 1 || kDefaultPChunks == 2, "P is published in 1 or 2 chunks");
 constexpr int kCausalGroup = 16;               // (batch, head) pairs ordered together (one item
                                                // per CTA, causal)
 
@@ -147,7 +168,7 @@ __device__ __forceinline__ uint4 pack8(const float* x, float scale) {
 // stored to TMEM columns [0, 64) of the row's S region, published in kChunks chunks (each chunk's
 // barrier completes when all 128 rows stored it). kPoly of every 8 pairs use the FMA-pipe
 // polynomial; the rest use the SFU.
-template <typename T, int kPoly, int kChunks>
+template <typename T, int kPoly, int kChunks, bool kPublish = true>
 __device__ __forceinline__ void softmax_exp_store(const float* sf, float sl2, float nref,
                                                   float (&ps)[4], uint32_t taddr_s,
                                                   uint64_t* chunk_bars) {
@@ -175,9 +196,11 @@ __device__ __forceinline__ void softmax_exp_store(const float* sf, float sl2, fl
       }
       tmem_st32(taddr_s + ch * (kPairsPerChunk) + q * 32, pk);
     }
-    tmem_st_wait();
-    tc_fence_before();
-    mbar_arrive(&chunk_bars[ch]);
+    if (kPublish) {
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&chunk_bars[ch]);
+    }
   }
 }
 
@@ -289,7 +312,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const WaitGuard guard{reinterpret_cast<volatile int*>(&sb->abort_flag), a.status};
 
   // Barrier phases run on across items: each role counts the completions it has waited for.
+  // Each role's branch starts with its side of the register split (every warp of a warpgroup
+  // executes the same setmaxnreg).
   if (warp == kProducerWarp) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(RegSplit<kPersistent>::kControl));
     // ------------------------------- TMA producer -------------------------------
     // Per item: Q tile 0, K_0, Q tile 1, V_0, K_1, V_1, ... (Q tile 0 and K_0 first, so tile 0's
     // first Q K^T waits for 64 KB). A Q buffer is reloaded for the next item as soon as the last
@@ -351,6 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp == kMmaWarp) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(RegSplit<kPersistent>::kControl));
     // ------------------------------- MMA issuer -------------------------------
     // The whole warp runs this loop (waits and descriptors stay warp-uniform); elect.sync picks
     // the one lane that issues each tcgen05.mma / commit. Across items, Q K^T of an item's first
@@ -461,6 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait(&sb->mma_done, 0, guard);
     }
   } else if (warp < kProducerWarp) {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(RegSplit<kPersistent>::kSoftmax));
     // ------------------------------- softmax warpgroups -------------------------------
     const int t = warp >> 2;                  // Q tile of this warpgroup
     const int quarter = warp & 3;             // TMEM lane quarter this warp may access
@@ -638,6 +666,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
     }
+  } else {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(RegSplit<kPersistent>::kControl));   // warps 10, 11
   }
 
   tc_fence_before();
@@ -665,6 +695,15 @@ int launch_variant(const PrefillArgs& a, const Maps& m, int grid, int dev, cudaS
                                                  kSmemBytes),
                             "cudaFuncSetAttribute(prefill)"))
       return st;
+    // The register split (setmaxnreg) draws on the registers the CTA is launched with; a build
+    // that launched with fewer than the split hands out would wait forever in setmaxnreg.inc.
+    cudaFuncAttributes attr{};
+    if (int st = check_cuda(cudaFuncGetAttributes(&attr, kernel), "cudaFuncGetAttributes(prefill)"))
+      return st;
+    if (attr.numRegs * kThreads <
+        2 * 128 * RegSplit<kPersistent>::kSoftmax + 128 * RegSplit<kPersistent>::kControl)
+      return fail(FLB_ERR_CUDA, "prefill kernel built with %d registers per thread, fewer than its "
+                  "register split needs", attr.numRegs);
     configured_device = dev;
   }
   kernel<<<grid, kThreads, kSmemBytes, stream>>>(a, m.q, m.k, m.v, m.o);
@@ -694,6 +733,14 @@ int launch_prefill(const PrefillArgs& a, const Maps& m, int head_dim, int sm_cou
     const int grid = static_cast<int>(std::min<int64_t>(units, sm_count));
     return launch_variant<T, 64, kDefaultPolyPairs, true>(a, m, grid, dev, stream);
   }
+#if FLB_PREFILL_PERSISTENT_D128
+  {
+    const int64_t units = static_cast<int64_t>(a.batch) * a.heads *
+                          (a.causal ? (a.q_blocks + 1) / 2 : a.q_blocks);
+    const int grid = static_cast<int>(std::min<int64_t>(units, sm_count));
+    return launch_variant<T, 128, kDefaultPolyPairs, true>(a, m, grid, dev, stream);
+  }
+#endif
   const int grid = static_cast<int>(items);
   switch (poly_pairs()) {
     case 0: return launch_variant<T, 128, 0, false>(a, m, grid, dev, stream);

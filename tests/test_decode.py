@@ -331,3 +331,42 @@ def test_paged_against_the_oracle_gqa_d64(page):
     rounding = np.abs(torch.from_numpy(ref).to(torch.bfloat16).double().numpy() - ref).max()
     assert err <= 2 * rounding, (err, rounding)
     assert np.abs(host64(lse) - ref_lse).max() < 1e-3
+
+
+@pytest.mark.parametrize("fill", ["ones", "random"])
+def test_balanced_decode_ignores_workspace_contents(fill):
+    # Every partial slot a merge reads is written by the same call, so a workspace holding
+    # anything (here all-ones bytes, or random bytes) gives the same bits as a fresh one, call
+    # after call.
+    import ctypes
+
+    from flash_lab import _capi
+
+    lib = _capi.load()
+    gen = torch.Generator(device="cuda").manual_seed(22)
+    q, k_cache, v_cache, seq_lens = make_case((6, 32, 8, 3000, 128, [3000, 1, 0, 2500, 64, 777]),
+                                              torch.bfloat16, gen)
+    ref_o, ref_lse = flash_lab.decode(q, k_cache, v_cache, seq_lens, return_lse=True)
+    q3 = q[:, 0]
+    batch, heads, d = q3.shape
+    sm = torch.cuda.get_device_properties(0).multi_processor_count
+    splits = lib.flb_decode_num_splits(batch, heads, 8, d, k_cache.shape[1], sm)
+    ws = torch.empty(lib.flb_decode_workspace_bytes(batch, heads, d, splits), device="cuda",
+                     dtype=torch.uint8)
+    if fill == "ones":
+        ws.fill_(0xFF)
+    else:
+        ws.copy_(torch.randint(0, 256, ws.shape, device="cuda", generator=gen).to(torch.uint8))
+    for _ in range(3):
+        o = torch.empty_like(q3)
+        lse = torch.empty(batch, heads, device="cuda", dtype=torch.float32)
+        p = _capi.DecodeParams(
+            q3.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), o.data_ptr(), lse.data_ptr(),
+            seq_lens.data_ptr(), q3.stride(0), q3.stride(1),
+            k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
+            v_cache.stride(0), v_cache.stride(1), v_cache.stride(2),
+            o.stride(0), o.stride(1), batch, heads, 8, d, k_cache.shape[1], 0, _capi.FLB_BF16,
+            1.0 / d ** 0.5, ws.data_ptr(), ws.numel(), 0)
+        assert lib.flb_decode_fwd(ctypes.byref(p), torch.cuda.current_stream().cuda_stream) == 0
+        torch.cuda.synchronize()
+        assert torch.equal(o, ref_o[:, 0]) and torch.equal(lse, ref_lse)
