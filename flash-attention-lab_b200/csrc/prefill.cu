@@ -22,12 +22,13 @@
 //    probabilities stay <= 256 and the common case never touches O. The final O / l and the LSE
 //    are exact for any reference point.
 //  * Work items are 256 query rows of one (batch, head). Two launch forms of one kernel:
-//    - one item per CTA (head_dim 128): non-causal q-blocks of one (batch, head) are adjacent in
-//      launch order, so the CTAs running together share K/V in L2; causal CTAs run heaviest
-//      first across groups of 16 (batch, head) pairs. The epilogue stages O / l in the Q tile's
-//      shared-memory buffer (free by then) and writes it with TMA stores.
-//    - persistent CTAs, one per SM, each running a fixed sequence of items (head_dim 64, where
-//      the per-item start and end weigh more against the shorter GEMMs). Barrier phases continue
+//    - one item per CTA (non-causal head_dim 128): the q-blocks of one (batch, head) are
+//      adjacent in launch order, so the CTAs running together share K/V in L2 (causal launches
+//      of this form run heaviest first across groups of 16 (batch, head) pairs). The epilogue
+//      stages O / l in the Q tile's shared-memory buffer (free by then) and writes it with TMA
+//      stores.
+//    - persistent CTAs, one per SM, each running a fixed sequence of items (causal, and head_dim
+//      64, where the per-item start and end weigh more against the work). Barrier phases continue
 //      across items; the next item's Q tiles load as soon as the last Q K^T reading them
 //      completes and its K/V tiles stream on through the same ring. Causal work comes in units
 //      of two q-blocks of one head, the i-th heaviest with the i-th lightest, so every unit
@@ -72,17 +73,17 @@ struct Geometry {
 // Warps: softmax WG0 (0-3), WG1 (4-7), then WG2: producer (8), MMA issuer (9) and two warps with
 // no role (10, 11), which make WG2 a whole warpgroup for the register split: the launch gives
 // every thread 168 registers (384 x 168 = 64512 of the SM's 65536); WG2 then drops to
-// kControl and the softmax warpgroups rise to kSoftmax (2 x 128 x 216 + 128 x 72 = 64512). The
-// persistent form's control warps keep more state (item walk, per-buffer counts), so its split
-// is 208 / 88; each is the split with the fewest spills in ptxas's report.
+// kControl and the softmax warpgroups rise to kSoftmax (2 x 128 x 216 + 128 x 72 = 64512).
+// Measured on B200: 208 / 88 spills less in the persistent form but runs slower there (head_dim
+// 64: 712 -> 693 TFLOP/s), so both forms use 216 / 72.
 constexpr int kThreads = 384;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr int kLaunchRegs = 168;
 template <bool kPersistent>
 struct RegSplit {
-  static constexpr int kSoftmax = kPersistent ? 208 : 216;
-  static constexpr int kControl = kPersistent ? 88 : 72;
+  static constexpr int kSoftmax = 216;
+  static constexpr int kControl = 72;
   static_assert(2 * 128 * kSoftmax + 128 * kControl <= kThreads * kLaunchRegs,
                 "the register split must fit in the launch's registers");
 };
@@ -90,8 +91,9 @@ constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;      // log2 units: p <= 2^8 between rescales
 constexpr int kDefaultPolyPairs = 2;           // of every 8 score pairs, 2^x on the FMA pipe
 #ifndef FLB_PREFILL_PERSISTENT_D128
-#define FLB_PREFILL_PERSISTENT_D128 0   // head_dim 128 with persistent CTAs (measurement knob)
+#define FLB_PREFILL_PERSISTENT_D128 0   // non-causal head_dim 128 persistent too (measurement knob)
 #endif
+constexpr bool kPersistentD128 = FLB_PREFILL_PERSISTENT_D128 != 0;
 #ifndef FLB_PREFILL_P_CHUNKS
 #define FLB_PREFILL_P_CHUNKS 1
 #endif
@@ -722,7 +724,8 @@ int poly_pairs() {
   return value;
 }
 
-// head_dim 128: one item per CTA (measured faster there); head_dim 64: persistent CTAs.
+// head_dim 128: one item per CTA when non-causal, persistent CTAs when causal; head_dim 64:
+// persistent CTAs (each form measured faster where it is used).
 template <typename T>
 int launch_prefill(const PrefillArgs& a, const Maps& m, int head_dim, int sm_count, int dev,
                    cudaStream_t stream) {
@@ -733,14 +736,15 @@ int launch_prefill(const PrefillArgs& a, const Maps& m, int head_dim, int sm_cou
     const int grid = static_cast<int>(std::min<int64_t>(units, sm_count));
     return launch_variant<T, 64, kDefaultPolyPairs, true>(a, m, grid, dev, stream);
   }
-#if FLB_PREFILL_PERSISTENT_D128
-  {
+  if (a.causal || kPersistentD128) {
+    // Causal at head_dim 128: persistent CTAs, whose paired heavy / light units also even out
+    // the items' lengths (measured 1058 -> 1082 TFLOP/s at (4,32,32,4096,128); non-causal
+    // stays one item per CTA, 1212 against 1206 persistent).
     const int64_t units = static_cast<int64_t>(a.batch) * a.heads *
                           (a.causal ? (a.q_blocks + 1) / 2 : a.q_blocks);
     const int grid = static_cast<int>(std::min<int64_t>(units, sm_count));
     return launch_variant<T, 128, kDefaultPolyPairs, true>(a, m, grid, dev, stream);
   }
-#endif
   const int grid = static_cast<int>(items);
   switch (poly_pairs()) {
     case 0: return launch_variant<T, 128, 0, false>(a, m, grid, dev, stream);

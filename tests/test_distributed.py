@@ -480,8 +480,8 @@ def _peer_rank(rank, world, port, seed):
             torch.cuda.synchronize()
             assert torch.equal(o_g, o_ref) and torch.equal(lse_g, lse_ref), (rank, "graph", step)
         assert ex.read_status() == 0 and ex.steps() == 7
+        q, o = qg.clone(), o_g.clone()      # the oracle check below: the last replay's step
         del graph
-        q = qg
         ref = oracle.decode(q.double().cpu().numpy(), kc.double().cpu().numpy(),
                             vc.double().cpu().numpy(), lens.cpu().numpy())
         err = np.abs(o.double().cpu().numpy() - ref).max()
