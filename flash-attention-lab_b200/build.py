@@ -7,6 +7,10 @@ Every .cu / .cpp under csrc/ is compiled with
 and linked into flash_lab/libflash_lab_b200.so next to the Python package that loads it. The
 ptxas resource report (registers, spills, shared memory per kernel) goes to
 build/ptxas.txt. Rebuilds only when a source, header or this script is newer than the library.
+
+Then binding/torch_ops.cpp (host C++, no kernels) is compiled against PyTorch's headers with
+torch.utils.cpp_extension into flash_lab/_flash_lab_torch.so, linked to the library above: the
+binding flash_lab.ops uses for eager calls (ATen allocation + the C ABI, without ctypes).
 """
 
 from __future__ import annotations
@@ -25,6 +29,8 @@ CSRC = HERE / "csrc"
 INCLUDE = ROOT / "include"
 BUILD = HERE / "build"
 LIB = HERE / "flash_lab" / "libflash_lab_b200.so"
+BINDING_SRC = HERE / "binding" / "torch_ops.cpp"
+BINDING = HERE / "flash_lab" / "_flash_lab_torch.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-I", str(INCLUDE),
@@ -83,12 +89,43 @@ def build(force: bool = False, debug: bool = False, verbose: bool = False, defin
     tmp = lib.with_suffix(".so.tmp")
     # The CUDA runtime is linked statically; driver entry points (cuTensorMapEncodeTiled) are
     # resolved at run time through cudaGetDriverEntryPoint, so the library loads without a GPU.
-    cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *[str(o) for o, _ in results]]
+    cmd = [nvcc(), *ARCH, "-shared", "-Xlinker", f"-soname={LIB.name}", "-o", str(tmp),
+           *[str(o) for o, _ in results]]
     proc = subprocess.run(cmd, capture_output=True, text=True)
     if proc.returncode != 0:
         raise RuntimeError(f"link failed:\n{proc.stdout}\n{proc.stderr}")
     os.replace(tmp, lib)
     return lib
+
+
+def build_binding(force: bool = False) -> pathlib.Path:
+    """Compiles the PyTorch binding (binding/torch_ops.cpp) against the built library."""
+    deps = [BINDING_SRC, *INCLUDE.glob("*.h"), LIB, pathlib.Path(__file__)]
+    if not force and BINDING.exists() and all(d.stat().st_mtime <= BINDING.stat().st_mtime
+                                             for d in deps):
+        return BINDING
+    import ctypes
+
+    from torch.utils import cpp_extension
+
+    # cpp_extension.load imports the module from the build folder: the library it needs is found
+    # loaded already, by its SONAME (in the package, $ORIGIN finds it).
+    ctypes.CDLL(str(LIB), mode=ctypes.RTLD_GLOBAL)
+    build_dir = BUILD / "torch_binding"
+    build_dir.mkdir(parents=True, exist_ok=True)
+    cpp_extension.load(
+        name="_flash_lab_torch", sources=[str(BINDING_SRC)], build_directory=str(build_dir),
+        extra_include_paths=[str(INCLUDE)], with_cuda=True,
+        extra_cflags=["-O2", "-std=c++17"],
+        # Ninja turns "$$" into "$" and its shell keeps the backslashed "$": the runpath is a
+        # literal $ORIGIN, so the binding finds the library in its own folder.
+        extra_ldflags=[f"-L{LIB.parent}", "-lflash_lab_b200", "-Wl,-rpath,\\$$ORIGIN"],
+        verbose=False)
+    built = build_dir / "_flash_lab_torch.so"
+    tmp = BINDING.with_suffix(".so.tmp")
+    shutil.copyfile(built, tmp)
+    os.replace(tmp, BINDING)
+    return BINDING
 
 
 def main() -> int:
@@ -103,6 +140,8 @@ def main() -> int:
     lib = build(force=args.force, debug=args.debug, verbose=args.verbose, defines=args.defines,
                 out=args.out)
     print(lib)
+    if args.out is None:
+        print(build_binding(force=args.force))
     return 0
 
 

@@ -38,6 +38,19 @@ else:
     HAS_EXTENSION = True
     EXTENSION_ERROR = ""
 
+# The PyTorch binding of the same C ABI (binding/torch_ops.cpp, built next to the library): it
+# allocates with ATen and calls flb_prefill_fwd / flb_decode_fwd from C++, which takes the ctypes
+# marshalling off an eager call. It links the in-tree library, so it is used only when that is the
+# library loaded (FLASH_LAB_LIBRARY not pointing elsewhere); the ctypes path below is otherwise
+# the one that runs, with the same semantics.
+_NATIVE = None
+if HAS_EXTENSION and os.path.realpath(os.environ.get("FLASH_LAB_LIBRARY", str(_capi.LIB_PATH))) \
+        == os.path.realpath(_capi.LIB_PATH):
+    try:
+        from flash_lab import _flash_lab_torch as _NATIVE
+    except ImportError:
+        _NATIVE = None
+
 _DTYPE_CODE = {torch.bfloat16: _capi.FLB_BF16, torch.float16: _capi.FLB_FP16}
 # The decode kernels also take fp32 caches (the reference's fp32 decode); prefill does not.
 _DECODE_DTYPE_CODE = {**_DTYPE_CODE, torch.float32: _capi.FLB_FP32}
@@ -204,6 +217,12 @@ class _DeviceGuard:
 
 def _prefill(q, k, v, causal: bool, softmax_scale: float):
     lib = _require_library()
+    if _NATIVE is not None:
+        o, lse = _NATIVE.prefill(q, k, v, bool(causal), float(softmax_scale),
+                                 _status_ptr(q.device))
+        if DEBUG:
+            _check(_capi.FLB_OK, "flb_prefill_fwd", q.device)
+        return o, lse
     if q.dtype not in _DTYPE_CODE or k.dtype != q.dtype or v.dtype != q.dtype:
         raise RuntimeError(f"prefill takes bf16 or fp16 tensors of one dtype, got {q.dtype}")
     batch, seqlen_q, heads, head_dim = q.shape
@@ -231,6 +250,13 @@ def _prefill(q, k, v, causal: bool, softmax_scale: float):
 def _decode(q, k_cache, v_cache, seq_lens, softmax_scale: float, num_splits: int,
             allow_splits: bool, block_tables=None):
     lib = _require_library()
+    if _NATIVE is not None:
+        o, lse = _NATIVE.decode(q, k_cache, v_cache, seq_lens, block_tables,
+                                float(softmax_scale), int(num_splits), bool(allow_splits),
+                                _status_ptr(q.device), _sm_count(q.device))
+        if DEBUG:
+            _check(_capi.FLB_OK, "flb_decode_fwd", q.device)
+        return o, lse
     if q.dtype not in _DECODE_DTYPE_CODE:
         raise RuntimeError(f"decode takes bf16, fp16 or fp32, got {q.dtype}")
     if q.dim() != 3 or k_cache.dim() != 4:
@@ -339,16 +365,20 @@ _BUILT_OPS = frozenset(
 )
 
 
-def _eager_ok(args) -> bool:
-    """Plain tensors, eager mode, no torch function or dispatch mode active, no profiler (which
-    then records the flash_lab:: op by name)."""
+def _plain_eager() -> bool:
+    """Eager mode with no torch function or dispatch mode active and no profiler (which then
+    records the flash_lab:: op by name)."""
     if torch.compiler.is_compiling() or torch._C._is_torch_function_mode_enabled():
         return False
     if torch.autograd._profiler_enabled():
         return False
-    if _python_dispatch._get_current_dispatch_mode() is not None:
-        return False
-    return all(type(a) is torch.Tensor for a in args if isinstance(a, torch.Tensor))
+    return _python_dispatch._get_current_dispatch_mode() is None
+
+
+def _eager_ok(args) -> bool:
+    """Plain tensors in plain eager mode (_plain_eager)."""
+    return _plain_eager() and all(type(a) is torch.Tensor for a in args
+                                  if isinstance(a, torch.Tensor))
 
 
 def _call_op(name: str, *args):
@@ -361,6 +391,9 @@ def _call_op(name: str, *args):
 
 
 _SELECTED: dict[tuple, object] = {}
+# Plain eager decode calls (no block table) by input metadata: the binding's arguments after a
+# call with the same metadata passed validation (see decode()).
+_DECODE_CALLS: dict[tuple, tuple] = {}
 
 
 def _select_cached(kind: str, table: dict, impl: str, device: torch.device, key: tuple,
@@ -443,6 +476,18 @@ def decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, seq_le
     sync); the kernel clamps them to [0, S_max].
     num_splits=None lets the library choose the split count from the shapes only.
     """
+    fast_key = None
+    if (_NATIVE is not None and block_tables is None and not DEBUG and type(q) is torch.Tensor
+            and type(k_cache) is torch.Tensor and type(v_cache) is torch.Tensor
+            and type(seq_lens) is torch.Tensor and _plain_eager()):
+        fast_key = (q.shape, q.stride(), q.dtype, q.device, k_cache.shape, k_cache.stride(),
+                    k_cache.dtype, k_cache.device, v_cache.shape, v_cache.stride(),
+                    v_cache.dtype, v_cache.device, seq_lens.shape, seq_lens.stride(),
+                    seq_lens.dtype, seq_lens.device, softmax_scale, num_splits, impl)
+        hit = _DECODE_CALLS.get(fast_key)
+        if hit is not None:
+            out, lse = _NATIVE.decode(q, k_cache, v_cache, seq_lens, None, *hit)
+            return (out, lse) if return_lse else out
     q3, shape = check_decode_inputs(q, k_cache, v_cache, seq_lens, block_tables)
     scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(shape.head_dim)
     if num_splits is not None and num_splits < 1:
@@ -453,6 +498,16 @@ def decode(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, seq_le
                  f"{shape.heads_kv}, paged={shape.paged}"),
         lambda s: s.unsupported_reason(shape, q.dtype),
     )
+    if fast_key is not None:
+        # Validation and the implementation choice depend only on what the key holds (shapes,
+        # strides, dtypes, devices and the arguments), so later calls with the same key go
+        # straight to the binding with the same arguments (a [B, 1, H, D] q is passed as is; the
+        # binding returns o in its shape).
+        if len(_DECODE_CALLS) >= 4096:
+            _DECODE_CALLS.clear()
+        _DECODE_CALLS[fast_key] = (float(scale), int(num_splits or 0),
+                                   spec.op != "decode_inplace", _status_ptr(q.device),
+                                   _sm_count(q.device))
     if block_tables is None:
         out, lse = _call_op(spec.op, q3, k_cache, v_cache, seq_lens, scale, num_splits or 0)
     else:

@@ -233,3 +233,75 @@ def test_eager_fast_path_only_for_plain_eager_calls():
     with Function():
         assert not ops._eager_ok((x,))
     assert ops._eager_ok((x,))
+
+
+def test_ops_use_the_built_torch_binding():
+    # When the PyTorch binding of the C ABI is built next to the library, the ops call it (the
+    # ctypes path stays for a library taken from FLASH_LAB_LIBRARY).
+    import os
+
+    from flash_lab import _capi, ops
+
+    binding = _capi.LIB_PATH.parent / "_flash_lab_torch.so"
+    if not binding.exists() or not ops.HAS_EXTENSION or os.environ.get("FLASH_LAB_LIBRARY"):
+        pytest.skip("the binding is not built here")
+    assert ops._NATIVE is not None and ops._NATIVE.abi_version() == 3
+
+
+@pytest.mark.gpu
+def test_torch_binding_and_ctypes_paths_agree(monkeypatch):
+    # The binding and the ctypes path fill the same parameter blocks: same bits, and a
+    # rejection inside the library (rows not 16-byte aligned) gives the same message.
+    from flash_lab import ops
+
+    if ops._NATIVE is None:
+        pytest.skip("the binding is not built here")
+    gen = torch.Generator(device="cuda").manual_seed(6)
+    q = torch.randn(2, 300, 8, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+    k = torch.randn(2, 500, 2, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+    qd = torch.randn(3, 1, 16, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+    kc = torch.randn(3, 2048, 4, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+    lens = torch.tensor([2048, 1, 900], device="cuda", dtype=torch.int32)
+    bad_q = torch.empty(3, 8, 136, device="cuda", dtype=torch.bfloat16)[:, :, :128]
+    bad_q = bad_q.as_strided((3, 8, 128), (8 * 136 - 8, 136 - 1, 1))   # rows 270 bytes apart
+    results, messages = [], []
+    for native in (ops._NATIVE, None):
+        monkeypatch.setattr(ops, "_NATIVE", native)
+        results.append((flash_lab.attention(q, k, k, causal=True, return_lse=True),
+                        flash_lab.decode(qd, kc, kc, lens, return_lse=True)))
+        with pytest.raises(RuntimeError) as err:
+            ops._decode(bad_q, kc, kc, lens, 0.1, 0, True)
+        messages.append(str(err.value))
+    torch.cuda.synchronize()
+    (pa, da), (pb, db) = results
+    assert torch.equal(pa[0], pb[0]) and torch.equal(pa[1], pb[1])
+    assert torch.equal(da[0], db[0]) and torch.equal(da[1], db[1])
+    assert messages[0] == messages[1] and "16-byte aligned rows" in messages[0], messages
+
+
+@pytest.mark.gpu
+def test_repeated_eager_decode_calls_take_the_memoised_path():
+    # A plain eager decode whose input metadata was seen before goes straight to the binding:
+    # same bits and shapes as the first (validated) call, for [B, 1, H, D] and [B, H, D] queries,
+    # and inputs with other metadata still get the reference's validation errors.
+    from flash_lab import ops
+
+    if ops._NATIVE is None:
+        pytest.skip("the binding is not built here")
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    q4 = torch.randn(2, 1, 8, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+    kc = torch.randn(2, 3000, 2, 128, device="cuda", dtype=torch.bfloat16, generator=gen)
+    lens = torch.tensor([3000, 1234], device="cuda", dtype=torch.int32)
+    ops._DECODE_CALLS.clear()
+    for q in (q4, q4[:, 0]):
+        first = flash_lab.decode(q, kc, kc, lens, return_lse=True)
+        second = flash_lab.decode(q, kc, kc, lens, return_lse=True)
+        third = flash_lab.decode(q, kc, kc, lens, num_splits=1, return_lse=True)
+        assert second[0].shape == q.shape == first[0].shape
+        assert torch.equal(first[0], second[0]) and torch.equal(first[1], second[1])
+        torch.testing.assert_close(third[0], first[0], atol=2e-2, rtol=0)
+    assert len(ops._DECODE_CALLS) == 4
+    with pytest.raises(TypeError, match="seq_lens must be int32"):
+        flash_lab.decode(q4, kc, kc, lens.long())
+    with pytest.raises(ValueError, match="num_splits must be positive"):
+        flash_lab.decode(q4, kc, kc, lens, num_splits=0)
