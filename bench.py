@@ -537,6 +537,8 @@ def main() -> int:
     ap.add_argument("--batch", type=int, default=None, help="batch size of --profile")
     ap.add_argument("--e2e-llama", action="store_true",
                     help="only the end-to-end Llama-3.1-8B-architecture generation")
+    ap.add_argument("--host-time", action="store_true",
+                    help="only the host time of eager decode calls (short-context latency)")
     ap.add_argument("--new-tokens", type=int, default=256)
     ap.add_argument("--prompt-len", type=int, default=8192)
     args = ap.parse_args()
@@ -544,6 +546,9 @@ def main() -> int:
         return run_profile_case(args)
     if args.e2e_llama:
         emit(run_e2e_llama(args))
+        return 0
+    if args.host_time:
+        emit(run_host_time())
         return 0
     if args.warmup < 3:
         args.warmup = 3
@@ -1033,6 +1038,71 @@ def run_e2e_llama(args) -> dict:
             "greedy_tokens_equal": agree, "greedy_tokens": args.new_tokens,
             "first_divergence": first_diff,
             "wall_s": time.perf_counter() - t_start}
+
+
+def run_host_time() -> dict:
+    """Host time of an eager flash_lab.decode call at short contexts (B=1 and B=8, H=32, head_dim
+    128, 512 to 4096 keys): 400 back-to-back calls after warm-up, best of five windows, with the
+    device time of the same call (a CUDA-graph replay) beside it. The host time is the cost of
+    the Python API, its validation and the launch; above the device time, a short-context decode
+    loop that does not capture graphs is bound by the host."""
+    import torch
+
+    import flash_lab
+
+    device = torch.device("cuda", 0)
+
+    def per_call_us(fn, n=400, reps=5):
+        best = float("inf")
+        for _ in range(reps):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(n):
+                fn()
+            t1 = time.perf_counter()
+            torch.cuda.synchronize()
+            best = min(best, (t1 - t0) / n * 1e6)
+        return best
+
+    rows = []
+    for batch, heads_kv in ((1, 32), (8, 8)):
+        for keys in (512, 2048, 4096):
+            gen = torch.Generator(device=device).manual_seed(3)
+            q = torch.randn(batch, 1, 32, 128, device=device, dtype=torch.bfloat16, generator=gen)
+            kc = torch.randn(batch, keys, heads_kv, 128, device=device, dtype=torch.bfloat16,
+                             generator=gen)
+            lens = torch.full((batch,), keys, device=device, dtype=torch.int32)
+
+            def call():
+                return flash_lab.decode(q, kc, kc, lens)
+
+            for _ in range(20):
+                call()
+            host = per_call_us(call)
+            graph = torch.cuda.CUDAGraph()
+            stream = torch.cuda.Stream(device)
+            stream.wait_stream(torch.cuda.current_stream(device))
+            with torch.cuda.stream(stream):
+                with torch.cuda.graph(graph, stream=stream):
+                    call()
+            torch.cuda.current_stream(device).wait_stream(stream)
+            for _ in range(10):
+                graph.replay()
+            st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            st.record()
+            for _ in range(200):
+                graph.replay()
+            en.record()
+            torch.cuda.synchronize(device)
+            rows.append({"batch": batch, "heads": 32, "heads_kv": heads_kv, "keys": keys,
+                         "host_us_per_call": host,
+                         "device_us_per_call": st.elapsed_time(en) / 200 * 1e3})
+            del graph
+    return {"metric": "eager flash_lab.decode host time per call (us, lower is better)",
+            "higher_is_better": False, "dtype": "bf16", "data": "synthetic",
+            "method": "400 back-to-back eager calls after 20 warm-up calls, best of 5 windows; "
+                      "device time from 200 CUDA-graph replays of the same call",
+            "rows": rows}
 
 
 def run_profile_case(args) -> int:
