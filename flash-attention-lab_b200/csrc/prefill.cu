@@ -95,7 +95,7 @@ constexpr int kDefaultPolyPairs = 2;           // of every 8 score pairs, 2^x on
 #endif
 constexpr bool kPersistentD128 = FLB_PREFILL_PERSISTENT_D128 != 0;
 #ifndef FLB_PREFILL_P_CHUNKS
-#define FLB_PREFILL_P_CHUNKS 1
+#define FLB_PREFILL_P_CHUNKS 2
 #endif
 constexpr int kDefaultPChunks = FLB_PREFILL_P_CHUNKS;   // P published to the MMA warp in this
                                                         // many chunks (1 or 2)
@@ -145,16 +145,41 @@ __device__ __forceinline__ void load_tile(uint8_t* dst, const CUtensorMap* map,
   }
 }
 
-// K-major SW128 operand (Q or K tile): k-step kk (16 elements) of a [128 x D] tile.
-__device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile_addr, int kk) {
-  return umma_smem_desc_sw128(tile_addr + (kk >> 2) * kBoxBytes + (kk & 3) * 32, 16, 1024);
+// Shared-memory operand descriptors, kept as their two 32-bit words. Within a tile, and from one
+// tile of the K/V ring or the Q buffers to the next, only the start-address field changes (the
+// address >> 4, bits 0-13 of the low word), and an add to it never carries out of the field
+// because shared-memory addresses stay below 2^18 bytes. So the MMA issuer derives the
+// descriptor of any k-step of any tile from one base descriptor with a single add: one UMMA
+// every 64 clocks (a 128 x 128 x 16 step) leaves the issuing warp no room for the full
+// descriptor arithmetic (measured on B200: SS and TS GEMMs of 128 x 128 x 128 issued
+// alternately take 727 clocks each with per-step descriptor construction, 514 with this).
+struct Desc {
+  uint32_t lo, hi;
+  __device__ __forceinline__ explicit Desc(uint64_t d)
+      : lo(static_cast<uint32_t>(d)), hi(static_cast<uint32_t>(d >> 32)) {}
+  __device__ __forceinline__ Desc(uint32_t l, uint32_t h) : lo(l), hi(h) {}
+  // The descriptor `bytes` further on in shared memory (bytes a multiple of 16).
+  __device__ __forceinline__ Desc at(uint32_t bytes) const { return Desc(lo + (bytes >> 4), hi); }
+  __device__ __forceinline__ uint64_t u64() const {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+  }
+};
+
+// K-major SW128 operand (Q or K tile): the descriptor of k-step 0 of the tile at tile_addr, and
+// the byte offset of k-step kk (16 elements) of a [128 x D] tile.
+__device__ __forceinline__ Desc kmajor_desc(uint32_t tile_addr) {
+  return Desc(umma_smem_desc_sw128(tile_addr, 16, 1024));
 }
+constexpr uint32_t kmajor_step(int kk) { return (kk >> 2) * kBoxBytes + (kk & 3) * 32; }
 
 // MN-major SW128 operand (V tile, N = head_dim): k-step kk covers keys 16kk..16kk+15; the
 // leading byte offset steps to the next 64 columns of N (unused at D = 64).
-__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile_addr, int kk) {
-  return umma_smem_desc_sw128(tile_addr + kk * 2048, kBoxBytes, 1024);
+__device__ __forceinline__ Desc mnmajor_desc(uint32_t tile_addr) {
+  return Desc(umma_smem_desc_sw128(tile_addr, kBoxBytes, 1024));
 }
+constexpr uint32_t mnmajor_step(int kk) { return kk * 2048; }
 
 template <typename T>
 __device__ __forceinline__ uint4 pack8(const float* x, float scale) {
@@ -381,8 +406,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kMmaWarp) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(RegSplit<kPersistent>::kControl));
     // ------------------------------- MMA issuer -------------------------------
-    // The whole warp runs this loop (waits and descriptors stay warp-uniform); elect.sync picks
-    // the one lane that issues each tcgen05.mma / commit. Across items, Q K^T of an item's first
+    // The whole warp runs this loop (waits stay warp-uniform); one lane, elected once, issues
+    // every tcgen05.mma and commit, so each commit tracks all the MMAs before it. Descriptors
+    // come from three base descriptors by one add each (Desc). Across items, Q K^T of an item's first
     // KV tile follows P V of the previous item's last one for the same Q tile: MMAs of one thread
     // run in issue order, so it cannot overwrite P before P V reads it. P V with accumulate = 0
     // overwrites O only after the softmax warpgroup has published the new item's first P, which
@@ -390,8 +416,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kFmt = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
     constexpr uint32_t kIdescQK = umma_idesc_f16(kFmt, kBM, kBN, 0);
     constexpr uint32_t kIdescPV = umma_idesc_f16(kFmt, kBM, D, 1);
-    const uint32_t q_addr = smem_u32(q_smem);
-    const uint32_t ring_addr = smem_u32(ring);
+    const bool leader = elect_one();
+    const Desc q_desc = kmajor_desc(smem_u32(q_smem));
+    const Desc ring_k = kmajor_desc(smem_u32(ring));
+    const Desc ring_v = mnmajor_desc(smem_u32(ring));
+    auto commit = [&](uint64_t* bar) {
+      if (leader) umma_commit(bar);
+    };
     int consumed = 0;                 // ring index of the item's K_0
     int q_waits[kQTiles] = {};
     int p_waits[kQTiles] = {};
@@ -400,13 +431,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto wait_ring = [&](int i) {
       return __all_sync(0xffffffffu, mbar_wait(&sb->kv_full[i % kSlots], (i / kSlots) & 1, guard));
     };
-    auto issue_qk = [&](int t, uint32_t k_addr) {
+    auto issue_qk = [&](int t, int k_slot) {
+      if (leader) {
+        const Desc qd = q_desc.at(t * kTileBytes);
+        const Desc kd = ring_k.at(k_slot * kTileBytes);
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        umma_ss_elect(tmem + t * 128, kmajor_desc(q_addr + t * kTileBytes, kk),
-                      kmajor_desc(k_addr, kk), kIdescQK, kk > 0);
+        for (int kk = 0; kk < D / 16; ++kk) {
+          umma_ss(tmem + t * 128, qd.at(kmajor_step(kk)).u64(), kd.at(kmajor_step(kk)).u64(),
+                  kIdescQK, kk > 0);
+        }
+        umma_commit(&sb->s_full[t]);
       }
-      umma_commit_elect(&sb->s_full[t]);
     };
     Item it;
     for (int k = 0; ok && item_at<kPersistent>(a, k, it); ++k) {
@@ -427,11 +462,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         ++q_waits[t];
         tc_fence_after();
-        issue_qk(t, ring_addr + (kbase % kSlots) * kTileBytes);
-        if (kPersistent && n_kv_tile[t] == 1) umma_commit_elect(&sb->q_free[t]);   // last Q K^T
+        issue_qk(t, kbase % kSlots);
+        if (kPersistent && n_kv_tile[t] == 1) commit(&sb->q_free[t]);   // last Q K^T
       }
       if (!ok) break;
-      umma_commit_elect(&sb->kv_empty[kbase % kSlots]);
+      commit(&sb->kv_empty[kbase % kSlots]);
       for (int j = 0; j < n_kv && ok; ++j) {
         const int iv = kbase + 2 * j + 1;  // V_j ring index
         const int sv = iv % kSlots;
@@ -439,8 +474,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int sk = ik % kSlots;
         ok = wait_ring(iv);
         if (!ok) break;
-        const uint32_t v_addr = ring_addr + sv * kTileBytes;
-        const uint32_t k_addr = ring_addr + sk * kTileBytes;
         bool k_ready = false;
 #pragma unroll
         for (int t = 0; t < kQTiles; ++t) {
@@ -452,11 +485,14 @@ __global__ void __launch_bounds__(kThreads, 1)
               ok = __all_sync(0xffffffffu, mbar_wait(&sb->p_half[t][ch], p_waits[t] & 1, guard));
               if (!ok) break;
               tc_fence_after();
+              if (leader) {
+                const Desc vd = ring_v.at(sv * kTileBytes);
 #pragma unroll
-              for (int kq = 0; kq < kBN / 16 / kPChunks; ++kq) {
-                const int kk = ch * (kBN / 16 / kPChunks) + kq;
-                umma_ts_elect(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
-                              mnmajor_desc(v_addr, kk), kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+                for (int kq = 0; kq < kBN / 16 / kPChunks; ++kq) {
+                  const int kk = ch * (kBN / 16 / kPChunks) + kq;
+                  umma_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8,
+                          vd.at(mnmajor_step(kk)).u64(), kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+                }
               }
             }
             if (!ok) break;
@@ -464,7 +500,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           // V_j is released once the last tile that uses it (always tile 1, whose range is the
           // item's) has its PV issued; K_{j+1} once tile 1's S for it is issued.
-          if (t == kQTiles - 1) umma_commit_elect(&sb->kv_empty[sv]);
+          if (t == kQTiles - 1) commit(&sb->kv_empty[sv]);
           if (j + 1 < n_kv_tile[t]) {
             if (!k_ready) {
               ok = wait_ring(ik);
@@ -472,21 +508,21 @@ __global__ void __launch_bounds__(kThreads, 1)
               tc_fence_after();
               k_ready = true;
             }
-            issue_qk(t, k_addr);
+            issue_qk(t, sk);
             if (kPersistent && j + 2 == n_kv_tile[t]) {
-              umma_commit_elect(&sb->q_free[t]);   // its last Q K^T
+              commit(&sb->q_free[t]);   // its last Q K^T
             }
           } else if (j + 1 == n_kv_tile[t]) {
-            umma_commit_elect(&sb->o_full[t]);
+            commit(&sb->o_full[t]);
           }
-          if (t == kQTiles - 1 && j + 1 < n_kv) umma_commit_elect(&sb->kv_empty[sk]);
+          if (t == kQTiles - 1 && j + 1 < n_kv) commit(&sb->kv_empty[sk]);
         }
       }
       consumed = kbase + 2 * n_kv;
     }
     // Every MMA issued has completed before TMEM may be released.
     if (issued_any) {
-      umma_commit_elect(&sb->mma_done);
+      commit(&sb->mma_done);
       mbar_wait(&sb->mma_done, 0, guard);
     }
   } else if (warp < kProducerWarp) {

@@ -262,6 +262,17 @@ __device__ __forceinline__ void umma_ts_elect(uint32_t d_tmem, uint32_t a_tmem, 
       : "memory");
 }
 
+// True on exactly one lane of a fully active warp (elect.sync's leader).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, e;\n\t}"
+      : "=r"(r));
+  return r != 0;
+}
+
 __device__ __forceinline__ void umma_commit_elect(uint64_t* bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\t"
