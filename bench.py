@@ -708,36 +708,50 @@ def run_extra(torch, flash_lab, device, dist, world, rank, args, peaks, traffic)
     from flash_lab.distributed import attention_sharded, prefill_pieces
 
     out = {}
+
+    def prefill_case(b, h, hkv, s, d, causal, seed, check_seed):
+        """One secondary prefill configuration, sharded like the headline: oracle check on
+        sampled rows, then the device-timed step (max over ranks)."""
+        gen = torch.Generator(device=device).manual_seed(seed)
+        q = torch.randn(b, s, h, d, device=device, dtype=torch.bfloat16, generator=gen)
+        k = torch.randn(b, s, hkv, d, device=device, dtype=torch.bfloat16, generator=gen)
+        v = torch.randn(b, s, hkv, d, device=device, dtype=torch.bfloat16, generator=gen)
+        scale = 1.0 / math.sqrt(d)
+        pieces = prefill_pieces(b, hkv, world, rank)
+        views = shard_views(q, k, v, pieces)
+        sp = attention_sharded(q, k, v, causal=causal, world_size=world, rank=rank)
+        rows = sample_rows(s, CHECK_ROWS, seed=check_seed)
+        check = gather_checks(merge_checks([check_prefill(o, lse, qq, kk, vv, causal, scale, rows)
+                                            for (o, lse), (qq, kk, vv) in zip(sp.outputs, views)]),
+                              dist)
+        del sp
+        flops = prefill_flops(b, h, s, s, d, causal)
+        rank_flops = sum(prefill_flops(qq.shape[0], qq.shape[2], s, s, d, causal)
+                         for qq, _, _ in views)
+
+        def step():
+            for qq, kk, vv in views:
+                flash_lab.attention(qq, kk, vv, causal=causal, softmax_scale=scale)
+
+        ms_rank, ms = time_steps(step, args.steps, args.warmup, dist, device)
+        achieved = rank_flops / (ms_rank * 1e-3) / 1e12 if rank_flops else 0.0
+        return {"value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+                "roofline_frac": achieved / peaks["bf16_tflops"], "flop_per_call": flops,
+                "scaling": "strong", "check": check}
+
     b, h, hkv, s, d = (PREFILL[x] for x in ("batch", "heads", "heads_kv", "seqlen", "head_dim"))
-    gen = torch.Generator(device=device).manual_seed(99)
-    q = torch.randn(b, s, h, d, device=device, dtype=torch.bfloat16, generator=gen)
-    k = torch.randn(b, s, hkv, d, device=device, dtype=torch.bfloat16, generator=gen)
-    v = torch.randn(b, s, hkv, d, device=device, dtype=torch.bfloat16, generator=gen)
-    scale = 1.0 / math.sqrt(d)
-    pieces = prefill_pieces(b, hkv, world, rank)
-    views = shard_views(q, k, v, pieces)
-    sp = attention_sharded(q, k, v, causal=True, world_size=world, rank=rank)
-    rows = sample_rows(s, CHECK_ROWS, seed=8)
-    check = gather_checks(merge_checks([check_prefill(o, lse, qq, kk, vv, True, scale, rows)
-                                        for (o, lse), (qq, kk, vv) in zip(sp.outputs, views)]),
-                          dist)
-    del sp
-    flops = prefill_flops(b, h, s, s, d, True)
-    rank_flops = sum(prefill_flops(qq.shape[0], qq.shape[2], s, s, d, True) for qq, _, _ in views)
-
-    def causal_step():
-        for qq, kk, vv in views:
-            flash_lab.attention(qq, kk, vv, causal=True, softmax_scale=scale)
-
-    ms_rank, ms = time_steps(causal_step, args.steps, args.warmup, dist, device)
-    achieved = rank_flops / (ms_rank * 1e-3) / 1e12 if rank_flops else 0.0
+    res = prefill_case(b, h, hkv, s, d, True, 99, 8)
     tr = traffic.get("prefill_kernel_causal")
-    out["prefill_causal"] = {"value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-                             "ms_per_step": ms, "roofline_frac": achieved / peaks["bf16_tflops"],
-                             "traffic": tr.get("bytes_per_launch") if tr else None,
-                             "flop_per_call": flops, "scaling": "strong", "check": check}
+    res["traffic"] = tr.get("bytes_per_launch") if tr else None
+    out["prefill_causal"] = res
     log(f"prefill causal: {out['prefill_causal']}")
-    del q, k, v, views
+    # head_dim 64, the reference's other head size, at the same tokens per launch (B = 8).
+    for causal in (False, True):
+        key = "prefill_d64_causal" if causal else "prefill_d64"
+        res = prefill_case(2 * b, h, hkv, s, 64, causal, 77, 9)
+        res["config"] = f"(B,H,H_kv,S,D)=({2 * b},{h},{hkv},{s},64) bf16 causal={causal}"
+        out[key] = res
+        log(f"{key}: {res}")
 
     l2_flush = torch.empty(512 * 2**20, dtype=torch.uint8, device=device)
     l2_drain = torch.zeros(128 * 2**20, dtype=torch.float32, device=device)   # 512 MB
