@@ -40,7 +40,9 @@ namespace {
 
 constexpr int kDecodeBK = 64;                       // keys per tile
 constexpr int kDecodeConsumerWarps = 4;             // 16 keys of each tile per warp
-constexpr int kDecodeThreads = (kDecodeConsumerWarps + 1) * 32;
+constexpr int kDecodeThreads = (kDecodeConsumerWarps + 1) * 32;   // fp32 kernel: one producer
+constexpr int kDecodeProducers = 2;                  // 16-bit kernel: a K warp and a V warp
+constexpr int kDecodeThreads16 = (kDecodeConsumerWarps + kDecodeProducers) * 32;
 constexpr int kMaxHeadsPerCta = 16;                 // M of the warp MMA
 constexpr int kMaxSplits = 256;
 constexpr int kMaxDest = FLB_MAX_PEERS;             // destinations of pushed partials
@@ -74,6 +76,8 @@ struct DecodeArgs {
   const int32_t* block_tables;
   int64_t bt_stride;
   int page_size, max_blocks, box_rows;
+  // 1: the K / V maps are two-half 5-D maps (16-bit, head_dim 128): one box per part of a tile.
+  int halves_map;
   int* status;
   int64_t q_batch_stride, q_head_stride;
   int64_t o_batch_stride, o_head_stride;
@@ -122,10 +126,12 @@ __device__ __forceinline__ int tma_c(const TmaCoords& c, int slot, int s, int h,
 }
 
 // The producer warp of both split kernels: streams ntiles tiles of kTileKeys keys (K then V) of
-// one (sequence b, KV head) starting at key k0 into the kStages ring. A tile is kColBoxes column
-// boxes (kColsPerBox columns, kColBoxBytes each in shared memory, rows of kRowBytes), each loaded
-// as kTileKeys / box_rows boxes of box_rows rows; lane i issues box i of the tile, so one warp
-// instruction issues them all. For a paged cache each box's block comes from the block table:
+// one (sequence b, KV head) starting at key k0 into the kStages ring. A tile is kTileKeys /
+// box_rows parts of box_rows rows (one page at most); a part is kColBoxes column boxes of
+// kColsPerBox columns (rows of kRowBytes), stored one after the other, so the tile's layout is
+// [part][column box][row in part]. With a two-half map one copy moves a whole part (both column
+// boxes), otherwise one copy per column box. Lane i issues copy i of the tile, so one warp
+// instruction issues them all (at most 32). For a paged cache each box's block comes from the block table:
 // the warp holds two windows of 32 entries (lane i: pages base + i and base + 32 + i), loading
 // the next window one window ahead, and each lane takes its box's entry by shuffle. Keys past
 // the split's end are still loaded (zeros or other blocks' rows) and masked by the consumers.
@@ -137,17 +143,21 @@ __device__ __forceinline__ int produce_kv(const DecodeArgs& a, const CUtensorMap
                                           const CUtensorMap* tmv, uint8_t* ring,
                                           uint64_t* full_bar, uint64_t* empty_bar, int k0,
                                           int ntiles, int hkv, int b, int t_base,
-                                          const WaitGuard& guard, int lane) {
+                                          const WaitGuard& guard, int lane, int kind_only) {
   constexpr int kStageBytes = 2 * kTileBytes;
   if (ntiles <= 0) return t_base;
   const bool paged = a.block_tables != nullptr;
   const int box_rows = paged ? a.box_rows : kTileKeys;
   const int parts = kTileKeys / box_rows;               // boxes along the keys of one tile
-  const int boxes = 2 * parts * kColBoxes;              // K and V boxes of one tile (<= 32)
-  // This lane's box: kind (0 = K, 1 = V), part j along the keys, column box cb.
-  const int kind = lane / (parts * kColBoxes);
-  const int j = (lane / kColBoxes) % parts;
-  const int cb = lane % kColBoxes;
+  const bool halves = a.halves_map != 0;
+  const int per_part = halves ? 1 : kColBoxes;          // copies per part
+  const int kinds = kind_only < 0 ? 2 : 1;              // K and V, or only kind_only
+  const int boxes = kinds * parts * per_part;           // copies of one tile by this warp (<= 32)
+  // This lane's copy: kind (0 = K, 1 = V), part j along the keys, column box cb.
+  const int kind = kind_only < 0 ? lane / (parts * per_part) : kind_only;
+  const int j = (lane / per_part) % parts;
+  const int cb = lane % per_part;
+  const int part_bytes = kColBoxes * box_rows * kRowBytes;
   const CUtensorMap* map = kind == 0 ? tmk : tmv;
   const TmaCoords& crd = kind == 0 ? a.kc : a.vc;
   const int64_t bt_row = static_cast<int64_t>(b) * a.bt_stride;
@@ -183,12 +193,17 @@ __device__ __forceinline__ int produce_kv(const DecodeArgs& a, const CUtensorMap
       blk = idx < 32 ? from_cur : from_next;
       row = key - page * a.page_size;
     }
-    if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
+    if (lane == 0) mbar_arrive_expect_tx(&full_bar[s], kinds * kTileBytes);
     __syncwarp();
     if (lane < boxes) {
-      tma_load_4d(dst + cb * kColBoxBytes + j * box_rows * kRowBytes, map, &full_bar[s],
-                  cb * kColsPerBox, tma_c(crd, 1, row, hkv, blk), tma_c(crd, 2, row, hkv, blk),
-                  tma_c(crd, 3, row, hkv, blk));
+      uint8_t* box_dst = dst + j * part_bytes + cb * box_rows * kRowBytes;
+      if (halves) {
+        tma_load_5d(box_dst, map, &full_bar[s], 0, row, 0, tma_c(crd, 3, row, hkv, blk),
+                    tma_c(crd, 4, row, hkv, blk));
+      } else {
+        tma_load_4d(box_dst, map, &full_bar[s], cb * kColsPerBox, tma_c(crd, 1, row, hkv, blk),
+                    tma_c(crd, 2, row, hkv, blk), tma_c(crd, 3, row, hkv, blk));
+      }
     }
     issued = r + 1;
   }
@@ -410,7 +425,7 @@ __device__ __forceinline__ void finish_split(const DecodeArgs& a, const float* w
 
 
 template <typename T, int D, bool kDeep>
-__global__ void __launch_bounds__(kDecodeThreads)
+__global__ void __launch_bounds__(kDecodeThreads16, 2)
     decode_split_kernel(const __grid_constant__ DecodeArgs a,
                         const __grid_constant__ CUtensorMap tmk,
                         const __grid_constant__ CUtensorMap tmv) {
@@ -466,7 +481,7 @@ __global__ void __launch_bounds__(kDecodeThreads)
   if (threadIdx.x == 0) {
     *abort_flag = 0;
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full_bar[s], 1);
+      mbar_init(&full_bar[s], kDecodeProducers);
       mbar_init(&empty_bar[s], kDecodeConsumerWarps);
     }
     fence_barrier_init();
@@ -506,8 +521,11 @@ __global__ void __launch_bounds__(kDecodeThreads)
     return 1;
   };
 
-  if (warp == kDecodeConsumerWarps) {
-    // ---------------- producer warp ----------------
+  if (warp >= kDecodeConsumerWarps) {
+    // ---------------- producer warps: K tiles, V tiles ----------------
+    // Two warps halve the copies each issues per tile (the copy issue rate bounds small pages);
+    // both arrive on each full barrier with their own bytes and both wait on each empty one.
+    const int kind = warp - kDecodeConsumerWarps;
     int issued = 0;
     for (int sb = sb_begin; sb < sb_end; ++sb) {
       int k0 = 0, k1 = 0;
@@ -517,7 +535,7 @@ __global__ void __launch_bounds__(kDecodeThreads)
       const int nt = k1 > k0 ? (k1 - k0 + kDecodeBK - 1) / kDecodeBK : 0;
       issued = produce_kv<kDecodeBK, Cfg::kBoxes, 64, Cfg::kBoxBytes, 128, kStages,
                           Cfg::kTileBytes>(a, &tmk, &tmv, smem, full_bar, empty_bar, k0, nt, hkv,
-                                           sb, issued, guard, lane);
+                                           sb, issued, guard, lane, kind);
       if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
     }
     drain_kv<kStages>(full_bar, issued, guard, lane);
@@ -528,11 +546,19 @@ __global__ void __launch_bounds__(kDecodeThreads)
   const int g = lane >> 2;   // fragment row group
   const int t4 = lane & 3;   // thread in quad
   const uint32_t smem_base = smem_u32(smem);
-  // ldmatrix row addresses (lane-dependent parts), see sw128_offset.
+  // ldmatrix row addresses (lane-dependent parts). A tile is [part][column box][row in part]
+  // (produce_kv); within a column box, rows are 128 bytes with the 16-byte chunks swizzled by
+  // the row's low 3 bits (sw128_offset; parts are multiples of 8 rows).
   const uint32_t k_row = static_cast<uint32_t>(warp * 16 + (lane >> 4) * 8 + (lane & 7));
   const uint32_t k_chunk_lo = static_cast<uint32_t>((lane >> 3) & 1);
   const uint32_t v_row = static_cast<uint32_t>(warp * 16 + ((lane >> 3) & 1) * 8 + (lane & 7));
   const uint32_t v_chunk_lo = static_cast<uint32_t>(lane >> 4);
+  const uint32_t part_rows = static_cast<uint32_t>(a.box_rows);
+  const uint32_t colbox_bytes = part_rows * 128u;          // one column box of one part
+  auto row_base = [&](uint32_t r) {                         // row r's line in column box 0
+    return (r / part_rows) * (Cfg::kBoxes * colbox_bytes) + (r % part_rows) * 128u;
+  };
+  const uint32_t k_line = row_base(k_row), v_line = row_base(v_row);
   // Cross-warp merge area: the ring once a uniform launch has consumed it; its own area in a
   // balanced launch, whose producer is already loading the next segment.
   const int mrows = a.merge_rows;
@@ -589,7 +615,8 @@ __global__ void __launch_bounds__(kDecodeThreads)
 #pragma unroll
       for (int kk = 0; kk < kKSteps; ++kk) {
         const uint32_t ch = 2 * kk + k_chunk_lo;
-        const uint32_t addr = kbase + (ch >> 3) * Cfg::kBoxBytes + sw128_offset(k_row, ch & 7);
+        const uint32_t addr =
+            kbase + k_line + (ch >> 3) * colbox_bytes + (((ch & 7) ^ (k_row & 7)) << 4);
         uint32_t b0, b1, b2, b3;
         ldsm_x4(addr, b0, b1, b2, b3);
         mma_16816<T>(sc[0], qa[kk], b0, b1);
@@ -654,7 +681,8 @@ __global__ void __launch_bounds__(kDecodeThreads)
 #pragma unroll
       for (int jp = 0; jp < kNTiles / 2; ++jp) {
         const uint32_t ch = 2 * jp + v_chunk_lo;
-        const uint32_t addr = vbase + (ch >> 3) * Cfg::kBoxBytes + sw128_offset(v_row, ch & 7);
+        const uint32_t addr =
+            vbase + v_line + (ch >> 3) * colbox_bytes + (((ch & 7) ^ (v_row & 7)) << 4);
         uint32_t b0, b1, b2, b3;
         ldsm_x4_trans(addr, b0, b1, b2, b3);
         mma_16816<T>(o_acc[2 * jp], pa, b0 & vmask_lo, b1 & vmask_hi);
@@ -794,7 +822,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
   if (warp == kDecodeConsumerWarps) {
     // ---------------- producer warp: [32 keys x D] fp32 tiles ----------------
     const int issued = produce_kv<kF32BK, 1, D, Cfg::kTileBytes, D * 4, kStages, Cfg::kTileBytes>(
-        a, &tmk, &tmv, smem, full_bar, empty_bar, k0, ntiles, hkv, b, 0, guard, lane);
+        a, &tmk, &tmv, smem, full_bar, empty_bar, k0, ntiles, hkv, b, 0, guard, lane, -1);
     drain_kv<kStages>(full_bar, issued, guard, lane);
     return;
   }
@@ -1118,7 +1146,7 @@ int launch_split(const DecodeArgs& args, const CUtensorMap& tmk, const CUtensorM
     configured_device = dev;
   }
   const int smem = Cfg::kSmemBytes + (args.balanced ? Cfg::merge_bytes(args.merge_rows) : 0);
-  decode_split_kernel<T, D, kDeep><<<dim3(grid_x, grid_y), kDecodeThreads, smem, stream>>>(
+  decode_split_kernel<T, D, kDeep><<<dim3(grid_x, grid_y), kDecodeThreads16, smem, stream>>>(
       args, tmk, tmv);
   return check_cuda(cudaGetLastError(), "decode_split_kernel launch");
 }
@@ -1226,6 +1254,13 @@ int box_rows_for(const flb_decode_params* p) {
   return p->block_tables != nullptr ? std::min(tile, p->page_size) : tile;
 }
 
+// 16-bit caches with head_dim 128 are read through two-half maps: one TMA copy per part of a
+// tile instead of one per column box. With 16-row pages that halves the copies (16 -> 8 per
+// 64-key tile), and the producer's copy rate is what bounds small pages.
+bool uses_halves_map(const flb_decode_params* p) {
+  return p->dtype != FLB_FP32 && p->head_dim == 128;
+}
+
 int build_maps(const flb_decode_params* p, CUtensorMap* tmk, CUtensorMap* tmv, TmaCoords* kc,
                TmaCoords* vc) {
   const int esize = p->dtype == FLB_FP32 ? 4 : 2;
@@ -1250,6 +1285,10 @@ int build_maps(const flb_decode_params* p, CUtensorMap* tmk, CUtensorMap* tmv, T
   if (p->dtype == FLB_FP32) {   // [box_rows x D] fp32 boxes, unswizzled
     if (int st = encode_rows_map(tmk, kc, kv, box_rows, p->head_dim, FLB_FP32, false)) return st;
     return encode_rows_map(tmv, vc, vv, box_rows, p->head_dim, FLB_FP32, false);
+  }
+  if (uses_halves_map(p)) {
+    if (int st = encode_rows_x64x2_map(tmk, kc, kv, box_rows, p->dtype)) return st;
+    return encode_rows_x64x2_map(tmv, vc, vv, box_rows, p->dtype);
   }
   if (int st = encode_rows_x64_map(tmk, kc, kv, box_rows, p->dtype)) return st;
   return encode_rows_x64_map(tmv, vc, vv, box_rows, p->dtype);
@@ -1283,6 +1322,7 @@ DecodeArgs make_args(const flb_decode_params* p) {
     a.max_blocks = p->max_seqlen / p->page_size;
   }
   a.box_rows = box_rows_for(p);
+  a.halves_map = uses_halves_map(p) ? 1 : 0;
   a.merge_rows = kMaxHeadsPerCta;
   return a;
 }

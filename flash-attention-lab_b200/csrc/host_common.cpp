@@ -3,6 +3,7 @@
 
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -173,6 +174,67 @@ int encode_rows_map(CUtensorMap* map, TmaCoords* coords, const View4& v, int box
                 (unsigned long long)dims[2], (unsigned long long)dims[3],
                 (unsigned long long)strides[0], (unsigned long long)strides[1],
                 (unsigned long long)strides[2]);
+  }
+  return FLB_OK;
+}
+
+int encode_rows_x64x2_map(CUtensorMap* map, TmaCoords* coords, const View4& v, int box_rows,
+                          int dtype) {
+  if (!rows_16b_aligned(v)) {
+    return fail(FLB_ERR_MISALIGNED,
+                "tensor must have 16-byte aligned rows (data pointer and strides)");
+  }
+  if (v.size[3] != 128 || v.elem_bytes != 2 || dtype == FLB_FP32) {
+    return fail(FLB_ERR_INVALID_ARGUMENT, "two-half tensor map needs 16-bit head_dim 128");
+  }
+  auto encode = encoder();
+  if (encode == nullptr) {
+    return fail(FLB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable (%s)",
+                cudaGetErrorString(g_encode_err));
+  }
+  // H (2) and B (0) after the half dimension, by increasing stride; size-1 dims get a harmless
+  // 16-byte multiple stride.
+  int outer[2] = {2, 0};
+  auto eff = [&](int i) -> int64_t { return v.size[i] <= 1 ? INT64_MAX : v.stride[i]; };
+  if (eff(outer[1]) < eff(outer[0])) std::swap(outer[0], outer[1]);
+  auto bytes_of = [&](int i, int64_t fallback) -> cuuint64_t {
+    if (v.size[i] <= 1) return static_cast<cuuint64_t>(fallback);
+    return static_cast<cuuint64_t>(v.stride[i] * v.elem_bytes);
+  };
+  const int64_t row_bytes = v.stride[1] * v.elem_bytes;
+  const int64_t span = std::max<int64_t>(row_bytes * std::max<int64_t>(v.size[1], 1), 256);
+  cuuint64_t dims[5] = {64, static_cast<cuuint64_t>(v.size[1]), 2,
+                        static_cast<cuuint64_t>(v.size[outer[0]]),
+                        static_cast<cuuint64_t>(v.size[outer[1]])};
+  cuuint64_t strides[4];
+  strides[0] = v.size[1] <= 1 ? 256 : static_cast<cuuint64_t>(row_bytes);
+  strides[1] = 128;
+  strides[2] = bytes_of(outer[0], ((span + 15) / 16) * 16);
+  strides[3] = bytes_of(outer[1], ((static_cast<int64_t>(strides[2]) *
+                                    std::max<int64_t>(v.size[outer[0]], 1) + 15) / 16) * 16);
+  cuuint32_t box[5] = {64, static_cast<cuuint32_t>(box_rows), 2, 1, 1};
+  cuuint32_t elem_strides[5] = {1, 1, 1, 1, 1};
+  int8_t pos[3] = {0, 0, 0};
+  pos[1] = 1;
+  pos[outer[0]] = 3;
+  pos[outer[1]] = 4;
+  coords->pos_b = pos[0];
+  coords->pos_s = pos[1];
+  coords->pos_h = pos[2];
+  coords->pad = 0;
+  const CUtensorMapDataType type =
+      dtype == FLB_FP16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUresult r = encode(map, type, 5, const_cast<void*>(v.base), dims, strides, box, elem_strides,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    return fail(FLB_ERR_CUDA,
+                "cuTensorMapEncodeTiled failed (%d): dims 64,%llu,2,%llu,%llu strides "
+                "%llu,%llu,%llu,%llu bytes",
+                static_cast<int>(r), (unsigned long long)dims[1], (unsigned long long)dims[3],
+                (unsigned long long)dims[4], (unsigned long long)strides[0],
+                (unsigned long long)strides[1], (unsigned long long)strides[2],
+                (unsigned long long)strides[3]);
   }
   return FLB_OK;
 }

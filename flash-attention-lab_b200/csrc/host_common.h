@@ -47,6 +47,15 @@ int encode_rows_x64_map(CUtensorMap* map, TmaCoords* coords, const View4& v, int
 int encode_rows_map(CUtensorMap* map, TmaCoords* coords, const View4& v, int box_rows,
                     int box_cols, int dtype, bool swizzle128);
 
+// A 5-D map over a 16-bit `v` with head_dim 128 whose box moves a whole [box_rows x 128] tile in
+// one copy: dimensions [64 columns] x [S] x [2 column halves, stride 128 bytes] x [H, B ordered
+// by stride]. The box [64 x box_rows x 2] lands in shared memory as two 128-byte-swizzled
+// [box_rows x 64] halves, one after the other (the layout of two encode_rows_x64_map boxes).
+// Coordinates: slot 0 and slot 2 (the half) are 0; coords gives the slots of S (always 1), H
+// and B (3 and 4).
+int encode_rows_x64x2_map(CUtensorMap* map, TmaCoords* coords, const View4& v, int box_rows,
+                          int dtype);
+
 // The 16-byte row rule every kernel here relies on: base pointer and every stride of a dimension
 // longer than 1 are multiples of 16 bytes, and the head_dim stride is 1.
 bool rows_16b_aligned(const View4& v);
