@@ -41,8 +41,9 @@ namespace {
 constexpr int kDecodeBK = 64;                       // keys per tile
 constexpr int kDecodeConsumerWarps = 4;             // 16 keys of each tile per warp
 constexpr int kDecodeThreads = (kDecodeConsumerWarps + 1) * 32;   // fp32 kernel: one producer
-constexpr int kDecodeProducers = 2;                  // 16-bit kernel: a K warp and a V warp
-constexpr int kDecodeThreads16 = (kDecodeConsumerWarps + kDecodeProducers) * 32;
+// Threads of the 16-bit kernel with kProducers producer warps (2 for small pages: a K warp and a
+// V warp).
+constexpr int decode_threads(int producers) { return (kDecodeConsumerWarps + producers) * 32; }
 constexpr int kMaxHeadsPerCta = 16;                 // M of the warp MMA
 constexpr int kMaxSplits = 256;
 constexpr int kMaxDest = FLB_MAX_PEERS;             // destinations of pushed partials
@@ -78,6 +79,8 @@ struct DecodeArgs {
   int page_size, max_blocks, box_rows;
   // 1: the K / V maps are two-half 5-D maps (16-bit, head_dim 128): one box per part of a tile.
   int halves_map;
+  // Producer warps of the 16-bit kernel: 2 (one per kind) for caches of small pages, else 1.
+  int producers;
   int* status;
   int64_t q_batch_stride, q_head_stride;
   int64_t o_batch_stride, o_head_stride;
@@ -129,16 +132,18 @@ __device__ __forceinline__ int tma_c(const TmaCoords& c, int slot, int s, int h,
 // one (sequence b, KV head) starting at key k0 into the kStages ring. A tile is kTileKeys /
 // box_rows parts of box_rows rows (one page at most); a part is kColBoxes column boxes of
 // kColsPerBox columns (rows of kRowBytes), stored one after the other, so the tile's layout is
-// [part][column box][row in part]. With a two-half map one copy moves a whole part (both column
-// boxes), otherwise one copy per column box. Lane i issues copy i of the tile, so one warp
-// instruction issues them all (at most 32). For a paged cache each box's block comes from the block table:
+// [part][column box][row in part]. Lane i issues copy i of the tile, so one warp instruction
+// issues them all (at most 32). The small-page form (kSmallPageForm) may read through two-half
+// maps (a.halves_map: one copy moves a whole part, both column boxes) and may load one kind
+// only (kind_only 0 = K, 1 = V, for two producer warps); otherwise one warp loads K and V with
+// one copy per column box. For a paged cache each box's block comes from the block table:
 // the warp holds two windows of 32 entries (lane i: pages base + i and base + 32 + i), loading
 // the next window one window ahead, and each lane takes its box's entry by shuffle. Keys past
 // the split's end are still loaded (zeros or other blocks' rows) and masked by the consumers.
 // The ring position continues from t_base tiles (earlier segments of the same CTA); returns the
 // ring position after the tiles it issued.
 template <int kTileKeys, int kColBoxes, int kColsPerBox, int kColBoxBytes, int kRowBytes,
-          int kStages, int kTileBytes>
+          int kStages, int kTileBytes, bool kSmallPageForm = false>
 __device__ __forceinline__ int produce_kv(const DecodeArgs& a, const CUtensorMap* tmk,
                                           const CUtensorMap* tmv, uint8_t* ring,
                                           uint64_t* full_bar, uint64_t* empty_bar, int k0,
@@ -149,8 +154,9 @@ __device__ __forceinline__ int produce_kv(const DecodeArgs& a, const CUtensorMap
   const bool paged = a.block_tables != nullptr;
   const int box_rows = paged ? a.box_rows : kTileKeys;
   const int parts = kTileKeys / box_rows;               // boxes along the keys of one tile
-  const bool halves = a.halves_map != 0;
+  const bool halves = kSmallPageForm && a.halves_map != 0;
   const int per_part = halves ? 1 : kColBoxes;          // copies per part
+  if (!kSmallPageForm) kind_only = -1;
   const int kinds = kind_only < 0 ? 2 : 1;              // K and V, or only kind_only
   const int boxes = kinds * parts * per_part;           // copies of one tile by this warp (<= 32)
   // This lane's copy: kind (0 = K, 1 = V), part j along the keys, column box cb.
@@ -424,8 +430,8 @@ __device__ __forceinline__ void finish_split(const DecodeArgs& a, const float* w
 }
 
 
-template <typename T, int D, bool kDeep>
-__global__ void __launch_bounds__(kDecodeThreads16, 2)
+template <typename T, int D, bool kDeep, int kProducers>
+__global__ void __launch_bounds__(decode_threads(kProducers), kProducers == 2 ? 2 : 0)
     decode_split_kernel(const __grid_constant__ DecodeArgs a,
                         const __grid_constant__ CUtensorMap tmk,
                         const __grid_constant__ CUtensorMap tmv) {
@@ -481,7 +487,7 @@ __global__ void __launch_bounds__(kDecodeThreads16, 2)
   if (threadIdx.x == 0) {
     *abort_flag = 0;
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full_bar[s], kDecodeProducers);
+      mbar_init(&full_bar[s], kProducers);
       mbar_init(&empty_bar[s], kDecodeConsumerWarps);
     }
     fence_barrier_init();
@@ -522,10 +528,11 @@ __global__ void __launch_bounds__(kDecodeThreads16, 2)
   };
 
   if (warp >= kDecodeConsumerWarps) {
-    // ---------------- producer warps: K tiles, V tiles ----------------
-    // Two warps halve the copies each issues per tile (the copy issue rate bounds small pages);
-    // both arrive on each full barrier with their own bytes and both wait on each empty one.
-    const int kind = warp - kDecodeConsumerWarps;
+    // ---------------- producer warps ----------------
+    // One warp loads K and V; with small pages two warps, one per kind, halve the copies each
+    // issues per tile (the copy issue rate bounds small pages). Both then arrive on each full
+    // barrier with their own bytes and both wait on each empty one.
+    const int kind = kProducers == 2 ? warp - kDecodeConsumerWarps : -1;
     int issued = 0;
     for (int sb = sb_begin; sb < sb_end; ++sb) {
       int k0 = 0, k1 = 0;
@@ -534,7 +541,8 @@ __global__ void __launch_bounds__(kDecodeThreads16, 2)
       if (st == 0) continue;
       const int nt = k1 > k0 ? (k1 - k0 + kDecodeBK - 1) / kDecodeBK : 0;
       issued = produce_kv<kDecodeBK, Cfg::kBoxes, 64, Cfg::kBoxBytes, 128, kStages,
-                          Cfg::kTileBytes>(a, &tmk, &tmv, smem, full_bar, empty_bar, k0, nt, hkv,
+                          Cfg::kTileBytes, kProducers == 2>(a, &tmk, &tmv, smem, full_bar,
+                                                            empty_bar, k0, nt, hkv,
                                            sb, issued, guard, lane, kind);
       if (__any_sync(0xffffffffu, *abort_flag != 0)) break;
     }
@@ -548,12 +556,13 @@ __global__ void __launch_bounds__(kDecodeThreads16, 2)
   const uint32_t smem_base = smem_u32(smem);
   // ldmatrix row addresses (lane-dependent parts). A tile is [part][column box][row in part]
   // (produce_kv); within a column box, rows are 128 bytes with the 16-byte chunks swizzled by
-  // the row's low 3 bits (sw128_offset; parts are multiples of 8 rows).
+  // the row's low 3 bits (sw128_offset; parts are multiples of 8 rows). Launches without small
+  // pages have one part per tile, whose column boxes are then compile-time kBoxBytes apart.
   const uint32_t k_row = static_cast<uint32_t>(warp * 16 + (lane >> 4) * 8 + (lane & 7));
   const uint32_t k_chunk_lo = static_cast<uint32_t>((lane >> 3) & 1);
   const uint32_t v_row = static_cast<uint32_t>(warp * 16 + ((lane >> 3) & 1) * 8 + (lane & 7));
   const uint32_t v_chunk_lo = static_cast<uint32_t>(lane >> 4);
-  const uint32_t part_rows = static_cast<uint32_t>(a.box_rows);
+  const uint32_t part_rows = kProducers == 2 ? static_cast<uint32_t>(a.box_rows) : kDecodeBK;
   const uint32_t colbox_bytes = part_rows * 128u;          // one column box of one part
   auto row_base = [&](uint32_t r) {                         // row r's line in column box 0
     return (r / part_rows) * (Cfg::kBoxes * colbox_bytes) + (r % part_rows) * 128u;
@@ -1129,15 +1138,15 @@ __global__ void decode_merge_balanced_kernel(const float* __restrict__ partial_o
   }
 }
 
-template <typename T, int D, bool kDeep>
-int launch_split(const DecodeArgs& args, const CUtensorMap& tmk, const CUtensorMap& tmv,
-                 int grid_x, int grid_y, cudaStream_t stream) {
+template <typename T, int D, bool kDeep, int kProducers>
+int launch_split_p(const DecodeArgs& args, const CUtensorMap& tmk, const CUtensorMap& tmv,
+                   int grid_x, int grid_y, cudaStream_t stream) {
   using Cfg = DecodeCfg<D, kDeep>;
   static thread_local int configured_device = -1;  // per-thread cache of the attribute set-up
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_device != dev) {
-    if (int st = check_cuda(cudaFuncSetAttribute(decode_split_kernel<T, D, kDeep>,
+    if (int st = check_cuda(cudaFuncSetAttribute(decode_split_kernel<T, D, kDeep, kProducers>,
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                  Cfg::kSmemBytes +
                                                      Cfg::merge_bytes(kMaxHeadsPerCta)),
@@ -1146,9 +1155,22 @@ int launch_split(const DecodeArgs& args, const CUtensorMap& tmk, const CUtensorM
     configured_device = dev;
   }
   const int smem = Cfg::kSmemBytes + (args.balanced ? Cfg::merge_bytes(args.merge_rows) : 0);
-  decode_split_kernel<T, D, kDeep><<<dim3(grid_x, grid_y), kDecodeThreads16, smem, stream>>>(
-      args, tmk, tmv);
+  decode_split_kernel<T, D, kDeep, kProducers>
+      <<<dim3(grid_x, grid_y), decode_threads(kProducers), smem, stream>>>(args, tmk, tmv);
   return check_cuda(cudaGetLastError(), "decode_split_kernel launch");
+}
+
+// Small pages (several parts per tile) run the two-producer form, everything else the
+// one-producer form whose consumers address one-part tiles with compile-time offsets.
+template <typename T, int D, bool kDeep>
+int launch_split(const DecodeArgs& args, const CUtensorMap& tmk, const CUtensorMap& tmv,
+                 int grid_x, int grid_y, cudaStream_t stream) {
+  if (args.producers == 2)
+    return launch_split_p<T, D, kDeep, 2>(args, tmk, tmv, grid_x, grid_y, stream);
+  if (args.box_rows != kDecodeBK)
+    return fail(FLB_ERR_UNSUPPORTED, "decode: pages under %d rows need the two-producer kernel",
+                kDecodeBK);
+  return launch_split_p<T, D, kDeep, 1>(args, tmk, tmv, grid_x, grid_y, stream);
 }
 
 template <typename T, bool kPeers = false>
@@ -1254,11 +1276,17 @@ int box_rows_for(const flb_decode_params* p) {
   return p->block_tables != nullptr ? std::min(tile, p->page_size) : tile;
 }
 
-// 16-bit caches with head_dim 128 are read through two-half maps: one TMA copy per part of a
-// tile instead of one per column box. With 16-row pages that halves the copies (16 -> 8 per
-// 64-key tile), and the producer's copy rate is what bounds small pages.
+// Caches of pages under one tile (8, 16 or 32 rows) need several TMA copies per tile, and the
+// producers' copy issue rate bounds them. With 16-bit head_dim 128 they are read through
+// two-half maps (one copy per page instead of one per 64-column box: 8 instead of 16 per 64-key
+// tile at 16-row pages) by two producer warps. Measured on the ragged GQA configuration with
+// 16-row pages: 121.9 -> 119.9 us. Contiguous caches keep one producer and 4-D maps, which
+// measured 1-4 % faster for them (short contexts most).
+bool has_small_pages(const flb_decode_params* p) {
+  return p->block_tables != nullptr && p->page_size < kDecodeBK;
+}
 bool uses_halves_map(const flb_decode_params* p) {
-  return p->dtype != FLB_FP32 && p->head_dim == 128;
+  return p->dtype != FLB_FP32 && p->head_dim == 128 && has_small_pages(p);
 }
 
 int build_maps(const flb_decode_params* p, CUtensorMap* tmk, CUtensorMap* tmv, TmaCoords* kc,
@@ -1323,6 +1351,7 @@ DecodeArgs make_args(const flb_decode_params* p) {
   }
   a.box_rows = box_rows_for(p);
   a.halves_map = uses_halves_map(p) ? 1 : 0;
+  a.producers = p->dtype != FLB_FP32 && has_small_pages(p) ? 2 : 1;
   a.merge_rows = kMaxHeadsPerCta;
   return a;
 }
@@ -1466,8 +1495,7 @@ BalancedPlan plan_balanced(const flb_decode_params* p, int splits, int columns, 
   // the deep ring, except for caches of small pages (under 64 rows), whose tiles are 8 to 16 TMA
   // boxes each: there one producer warp per SM cannot issue them fast enough (measured with
   // 16-row pages: 179 us with one CTA per SM, 157 us with more), so two CTAs share each SM.
-  const bool small_pages = p->block_tables != nullptr && p->page_size < kDecodeBK;
-  const int per_sm = small_pages && two_per_sm(smem2) ? 2 : 1;
+  const int per_sm = has_small_pages(p) && two_per_sm(smem2) ? 2 : 1;
   plan.deep = per_sm == 1;
   plan.ctas = std::clamp(per_sm * sm_count / columns, p->batch, 2 * p->batch * splits);
   plan.on = true;
