@@ -32,8 +32,10 @@
 //      across items; the next item's Q tiles load as soon as the last Q K^T reading them
 //      completes and its K/V tiles stream on through the same ring. Causal work comes in units
 //      of two q-blocks of one head, the i-th heaviest with the i-th lightest, so every unit
-//      costs the same and the static assignment stays balanced. The Q buffers are not free for
-//      staging here, so each softmax thread stores its O row directly.
+//      costs the same and the static assignment stays balanced; when K and V fit about in L2,
+//      single q-blocks are dealt out in cost order instead, back and forth over the CTAs, which
+//      balances item counts that are not multiples of the CTA count. The Q buffers are not free
+//      for staging here, so each softmax thread stores its O row directly.
 //  * Tiles past the diagonal are never loaded; tiles crossing it are masked element-wise.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -94,6 +96,12 @@ constexpr int kDefaultPolyPairs = 2;           // of every 8 score pairs, 2^x on
 #define FLB_PREFILL_PERSISTENT_D128 0   // non-causal head_dim 128 persistent too (measurement knob)
 #endif
 constexpr bool kPersistentD128 = FLB_PREFILL_PERSISTENT_D128 != 0;
+// Causal persistent launches whose K and V fit about in L2 schedule single items in cost order
+// (PrefillArgs::snake); larger ones keep heavy / light pairs of one head, whose CTAs share K/V
+// in L2. Measured on one B200 at the per-GPU shapes of (4, 32, 32, 4096, 128) sharded over N
+// GPUs (B x H = 128 / N heads; K+V 268 / 134 / 67 / 34 MB): pairs 492 / 276 / 151 / 81 us,
+// single items in cost order 559 / 264 / 136-145 / 70-77 us.
+constexpr int64_t kSnakeMaxKvBytes = int64_t{192} << 20;
 #ifndef FLB_PREFILL_P_CHUNKS
 #define FLB_PREFILL_P_CHUNKS 2
 #endif
@@ -111,6 +119,7 @@ struct PrefillArgs {
   int batch, seqlen_q, seqlen_k, heads, heads_kv, group;
   int causal, causal_offset;
   int q_blocks;
+  int snake;   // causal persistent: single items in cost order, boustrophedon over the CTAs
   float scale, scale_log2;
   TmaCoords qc, kc, vc, oc;
 };
@@ -269,6 +278,19 @@ __device__ __forceinline__ bool item_at(const PrefillArgs& a, int k, Item& it) {
     if (u >= static_cast<int64_t>(a.batch) * a.heads * a.q_blocks) return false;
     it.bh = static_cast<int>(u / a.q_blocks);
     it.qb = static_cast<int>(u - static_cast<int64_t>(it.bh) * a.q_blocks);
+    return true;
+  }
+  if (a.snake) {
+    // Item i of the cost order (all heads' last q-block, then all heads' second-to-last, ...):
+    // round k gives CTAs 0..G-1 items kG..kG+G-1 on even rounds and in reverse on odd ones,
+    // so every CTA's total stays close to the mean.
+    const int64_t total = static_cast<int64_t>(a.batch) * a.heads * a.q_blocks;
+    const int64_t pos = (k & 1) ? gridDim.x - 1 - blockIdx.x : blockIdx.x;
+    const int64_t i = static_cast<int64_t>(k) * gridDim.x + pos;
+    if (i >= total) return false;
+    const int64_t bhs = static_cast<int64_t>(a.batch) * a.heads;
+    it.qb = a.q_blocks - 1 - static_cast<int>(i / bhs);
+    it.bh = static_cast<int>(i - (i / bhs) * bhs);
     return true;
   }
   const int pairs = (a.q_blocks + 1) / 2;
@@ -767,8 +789,8 @@ int launch_prefill(const PrefillArgs& a, const Maps& m, int head_dim, int sm_cou
                    cudaStream_t stream) {
   const int64_t items = static_cast<int64_t>(a.batch) * a.heads * a.q_blocks;
   if (head_dim == 64) {
-    const int64_t units =
-        static_cast<int64_t>(a.batch) * a.heads * (a.causal ? (a.q_blocks + 1) / 2 : a.q_blocks);
+    const int64_t units = static_cast<int64_t>(a.batch) * a.heads *
+                          (a.causal && !a.snake ? (a.q_blocks + 1) / 2 : a.q_blocks);
     const int grid = static_cast<int>(std::min<int64_t>(units, sm_count));
     return launch_variant<T, 64, kDefaultPolyPairs, true>(a, m, grid, dev, stream);
   }
@@ -777,7 +799,7 @@ int launch_prefill(const PrefillArgs& a, const Maps& m, int head_dim, int sm_cou
     // the items' lengths (measured 1058 -> 1082 TFLOP/s at (4,32,32,4096,128); non-causal
     // stays one item per CTA, 1212 against 1206 persistent).
     const int64_t units = static_cast<int64_t>(a.batch) * a.heads *
-                          (a.causal ? (a.q_blocks + 1) / 2 : a.q_blocks);
+                          (a.causal && !a.snake ? (a.q_blocks + 1) / 2 : a.q_blocks);
     const int grid = static_cast<int>(std::min<int64_t>(units, sm_count));
     return launch_variant<T, 128, kDefaultPolyPairs, true>(a, m, grid, dev, stream);
   }
@@ -865,6 +887,9 @@ extern "C" int flb_prefill_fwd(const flb_attn_params* p, flb_stream_t stream_) {
   a.causal = p->causal ? 1 : 0;
   a.causal_offset = p->seqlen_k - p->seqlen_q;
   a.q_blocks = (p->seqlen_q + kRowsPerCta - 1) / kRowsPerCta;
+  const int64_t kv_bytes = static_cast<int64_t>(p->batch) * p->heads_kv * p->seqlen_k *
+                           p->head_dim * 2 * 2;
+  a.snake = (p->causal && kv_bytes <= kSnakeMaxKvBytes) ? 1 : 0;
   a.scale = p->softmax_scale;
   a.scale_log2 = static_cast<float>(static_cast<double>(p->softmax_scale) * 1.4426950408889634);
 
