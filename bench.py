@@ -532,7 +532,7 @@ def main() -> int:
                     help="skip the Llama-3.1-8B-architecture generation in the extras")
     ap.add_argument("--profile", default=None,
                     choices=["prefill", "prefill_causal", "decode_mha", "decode_gqa",
-                             "decode_gqa_ragged"],
+                             "decode_gqa_ragged", "decode_gqa_ragged_paged16"],
                     help="run only warmup + steps launches of one kernel (for ncu captures)")
     ap.add_argument("--batch", type=int, default=None, help="batch size of --profile")
     ap.add_argument("--e2e-llama", action="store_true",
@@ -1145,10 +1145,17 @@ def run_profile_case(args) -> int:
         kc = torch.randn(b, smax, hk, d, device=device, dtype=torch.bfloat16, generator=gen)
         vc = torch.randn(b, smax, hk, d, device=device, dtype=torch.bfloat16, generator=gen)
         lens = torch.full((b,), smax, device=device, dtype=torch.int32)
-        if args.profile == "decode_gqa_ragged":   # the bench's lengths, U[16384, 32768]
+        if args.profile.startswith("decode_gqa_ragged"):   # the bench's lengths, U[16384, 32768]
             lens = torch.randint(16384, smax + 1, (b,), generator=torch.Generator().manual_seed(0))
             lens = lens.to(device=device, dtype=torch.int32)
-        fn = lambda: flash_lab.decode(qd, kc, vc, lens)  # noqa: E731
+        tables = None
+        if args.profile.endswith("paged16"):   # the bench's pool of 16-row pages, shuffled
+            page, nb = 16, smax // 16
+            perm = torch.randperm(b * nb, device=device, generator=gen)
+            kc = kc.view(b * nb, page, hk, d)[torch.argsort(perm)]
+            vc = vc.view(b * nb, page, hk, d)[torch.argsort(perm)]
+            tables = perm.view(b, nb).to(torch.int32)
+        fn = lambda: flash_lab.decode(qd, kc, vc, lens, block_tables=tables)  # noqa: E731
         what = f"decode B={b} H=32 H_kv={hk} S=32768 D=128 lengths={lens.tolist()}"
     for _ in range(args.warmup + args.steps):
         fn()

@@ -1109,27 +1109,55 @@ __global__ void decode_merge_balanced_kernel(const float* __restrict__ partial_o
   const int64_t base = static_cast<int64_t>(h) * (batch + total) + b;   // + c: CTA c's slot
   asm volatile("griddepcontrol.wait;" ::: "memory");
   // CTA c (chunks [g(c), g(c + 1))) holds part of sequence b when that range meets [p0, p1).
+  // The holders' partials are read kMergeBatch at a time, all loads of a batch issued before
+  // any is used (each is an L2 round trip), and combined in CTA order as before.
+  constexpr int kMergeBatch = 8;
   float m = -INFINITY;
   {
     ChunkWalk w = walk0;
-    for (int c = c_first; c <= c_last; ++c) {
-      const int64_t g0 = w.g;
-      const int64_t g1 = w.step();
-      if (max(g0, p0) < min(g1, p1)) m = fmaxf(m, partial_ml[2 * (base + c)]);
+    for (int c0 = c_first; c0 <= c_last; c0 += kMergeBatch) {
+      float mv[kMergeBatch];
+#pragma unroll
+      for (int i = 0; i < kMergeBatch; ++i) {
+        const int c = c0 + i;
+        mv[i] = -INFINITY;
+        if (c <= c_last) {
+          const int64_t g0 = w.g;
+          const int64_t g1 = w.step();
+          if (max(g0, p0) < min(g1, p1)) mv[i] = partial_ml[2 * (base + c)];
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kMergeBatch; ++i) m = fmaxf(m, mv[i]);
     }
   }
   for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
     float num = 0.f, den = 0.f;
     ChunkWalk w = walk0;
-    for (int c = c_first; c <= c_last; ++c) {
-      const int64_t g0 = w.g;
-      const int64_t g1 = w.step();
-      if (!(max(g0, p0) < min(g1, p1))) continue;
-      const float ms = partial_ml[2 * (base + c)];
-      if (ms != -INFINITY) {
-        const float f = ex2(ms - m);
-        num += partial_o[(base + c) * head_dim + d] * f;
-        den += partial_ml[2 * (base + c) + 1] * f;
+    for (int c0 = c_first; c0 <= c_last; c0 += kMergeBatch) {
+      float ms[kMergeBatch], ls[kMergeBatch], os[kMergeBatch];
+#pragma unroll
+      for (int i = 0; i < kMergeBatch; ++i) {
+        const int c = c0 + i;
+        ms[i] = -INFINITY;
+        ls[i] = os[i] = 0.f;
+        if (c <= c_last) {
+          const int64_t g0 = w.g;
+          const int64_t g1 = w.step();
+          if (max(g0, p0) < min(g1, p1)) {
+            ms[i] = partial_ml[2 * (base + c)];
+            ls[i] = partial_ml[2 * (base + c) + 1];
+            os[i] = partial_o[(base + c) * head_dim + d];
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kMergeBatch; ++i) {
+        if (ms[i] != -INFINITY) {
+          const float f = ex2(ms[i] - m);
+          num += os[i] * f;
+          den += ls[i] * f;
+        }
       }
     }
     T* out = o + static_cast<int64_t>(b) * o_batch_stride + static_cast<int64_t>(h) * o_head_stride;
