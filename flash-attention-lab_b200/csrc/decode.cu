@@ -1060,16 +1060,37 @@ __global__ void decode_merge_kernel(const float* __restrict__ partial_o,
   }
   auto load = [](const float* p) { return kPeers ? __ldcg(p) : *p; };
   const int64_t base = static_cast<int64_t>(bh) * num_splits;
+  // Partials are read kMergeBatch at a time, a batch's loads issued before any is used, and
+  // combined in split order.
+  constexpr int kMergeBatch = 8;
   float m = -INFINITY;
-  for (int s = 0; s < num_splits; ++s) m = fmaxf(m, load(partial_ml + 2 * (base + s)));
+  for (int s0 = 0; s0 < num_splits; s0 += kMergeBatch) {
+    float mv[kMergeBatch];
+#pragma unroll
+    for (int i = 0; i < kMergeBatch; ++i)
+      mv[i] = s0 + i < num_splits ? load(partial_ml + 2 * (base + s0 + i)) : -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kMergeBatch; ++i) m = fmaxf(m, mv[i]);
+  }
   for (int d = threadIdx.x; d < head_dim; d += blockDim.x) {
     float num = 0.f, den = 0.f;
-    for (int s = 0; s < num_splits; ++s) {
-      const float ms = load(partial_ml + 2 * (base + s));
-      if (ms != -INFINITY) {
-        const float f = ex2(ms - m);
-        num += load(partial_o + (base + s) * head_dim + d) * f;
-        den += load(partial_ml + 2 * (base + s) + 1) * f;
+    for (int s0 = 0; s0 < num_splits; s0 += kMergeBatch) {
+      float ms[kMergeBatch], ls[kMergeBatch], os[kMergeBatch];
+#pragma unroll
+      for (int i = 0; i < kMergeBatch; ++i) {
+        const int64_t sl = base + s0 + i;
+        const bool in = s0 + i < num_splits;
+        ms[i] = in ? load(partial_ml + 2 * sl) : -INFINITY;
+        ls[i] = in ? load(partial_ml + 2 * sl + 1) : 0.f;
+        os[i] = in ? load(partial_o + sl * head_dim + d) : 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < kMergeBatch; ++i) {
+        if (ms[i] != -INFINITY) {
+          const float f = ex2(ms[i] - m);
+          num += os[i] * f;
+          den += ls[i] * f;
+        }
       }
     }
     T* out = o + static_cast<int64_t>(b) * o_batch_stride + static_cast<int64_t>(h) * o_head_stride;
