@@ -175,3 +175,17 @@ def test_head_dim_64_long_gqa_sampled_rows(causal):
     middle = torch.randperm(4094, generator=gen)[:254] + 1
     rows = torch.cat([torch.tensor([0, 4095]), middle]).sort().values
     check_prefill(out, lse, q, k, v, causal, rows=rows)
+
+
+def test_causal_schedules_agree_bitwise():
+    """Causal launches whose K/V exceed 192 MB run heavy/light q-block pairs per CTA, smaller ones
+    single q-blocks dealt in cost order; the schedule only decides which CTA runs an item. The
+    benchmark configuration (268 MB of K/V, pairs) must equal its two batch halves (134 MB each,
+    cost order) bit for bit."""
+    q, k, v = make_inputs((4, 4096, 4096, 32, 32, 128), torch.bfloat16, seed=3)
+    out, lse = flash_lab.attention(q, k, v, causal=True, return_lse=True)
+    for b0 in (0, 2):
+        part, part_lse = flash_lab.attention(q[b0:b0 + 2], k[b0:b0 + 2], v[b0:b0 + 2],
+                                             causal=True, return_lse=True)
+        assert torch.equal(part, out[b0:b0 + 2])
+        assert torch.equal(part_lse, lse[b0:b0 + 2])
