@@ -309,6 +309,27 @@ def test_paged_cache_matches_contiguous(impl, dtype, page):
     check_decode(out, lse, q, k_cache, v_cache, seq_lens)
 
 
+@pytest.mark.parametrize("page", [8, 16, 32])
+def test_paged_pool_head_major_strides(page):
+    # A pool stored [num_blocks, H_kv, page, D] and passed as its [num_blocks, page, H_kv, D]
+    # view: the small-page kernel's two-half tensor maps follow any strides that keep the
+    # 16-byte rows, and give bitwise the contiguous-pool result.
+    gen = torch.Generator(device="cuda").manual_seed(50 + page)
+    q, k_cache, v_cache, seq_lens = make_case((2, 32, 8, 2048, 128, [2048, 1333]),
+                                              torch.bfloat16, gen)
+    nb = 2048 // page
+    perm = torch.randperm(2 * nb, device="cuda", generator=gen).view(2, nb)
+    tables = perm.to(torch.int32)
+    kp, vp = to_paged(k_cache, page, perm), to_paged(v_cache, page, perm)
+    kh = kp.transpose(1, 2).contiguous().transpose(1, 2)   # same values, head-major storage
+    vh = vp.transpose(1, 2).contiguous().transpose(1, 2)
+    assert kh.stride(1) == 128 and kh.stride(2) == page * 128
+    ref_o, ref_lse = flash_lab.decode(q, kp, vp, seq_lens, block_tables=tables, return_lse=True)
+    out, lse = flash_lab.decode(q, kh, vh, seq_lens, block_tables=tables, return_lse=True)
+    assert torch.equal(out, ref_o) and torch.equal(lse, ref_lse)
+    check_decode(out, lse, q, k_cache, v_cache, seq_lens)
+
+
 @pytest.mark.parametrize("page", [16, 64])
 def test_paged_against_the_oracle_gqa_d64(page):
     # head_dim 64, GQA group 4, ragged lengths: the oracle reads the pool through the tables
